@@ -1,0 +1,13 @@
+"""Reference import path of the torch extension (``import afa_flash_attention_kernels as fa``).
+
+Re-exports the sm_100a extension built inside ampere_flash_attention_from_scratch_b200;
+``forward(kernel_cfg, q, k, v, o, benchmark=False) -> (O, runtime_ms)`` as in the
+reference binding (csrc/ampere_flash_attention.cu:138-141).
+"""
+
+from ampere_flash_attention_from_scratch_b200.afa_flash_attention_kernels import (  # noqa: F401
+    _raise_formatted_error,
+    check_status,
+    forward,
+    kernel_keys,
+)

@@ -1,0 +1,492 @@
+// afa_fwd_kernel.cuh -- Blackwell (sm_100a) FlashAttention forward kernel.
+//
+// Computes O = softmax(Q K^T * scale) V for one (batch, head) slice per work
+// item, non-causal, fp16/bf16 in, fp32 accumulate, fp16/bf16 out.  Same
+// operation as the reference's afa_forward_kernel
+// (csrc/include/afa_forward_kernel.cuh:18-202), re-designed for sm_100a:
+//
+//   * persistent grid (one CTA per SM) walking work items (b, h, q-pair);
+//     a q-pair is 256 query rows = two 128-row Q tiles;
+//   * warp 0      : TMA producer.  Q0/Q1 once per work item, then K_j, V_j
+//                   into a kStages-deep ring of 128-row slots (SWIZZLE_128B);
+//   * warp 1      : MMA issuer (one thread).  S_i = Q_i K_j^T and
+//                   O_i += P_i V_j with tcgen05.mma, completion via
+//                   tcgen05.commit -> mbarrier;
+//   * warp 2      : TMEM allocator (512 columns: S0 | S1 | O0 | O1);
+//   * warps 4-7   : softmax warpgroup 0 (Q tile 0), warps 8-11: warpgroup 1.
+//                   One thread owns one query row (one TMEM lane): row max,
+//                   exp2, row sum and the final 1/l need no shuffles.  P is
+//                   written back into TMEM over S and consumed from TMEM by
+//                   the PV MMA.  O is rescaled in TMEM only when a row max
+//                   grows by more than 2^8 (conditional rescaling).
+//
+// The MMA issue order  PV0(j-1), S0(j), PV1(j-1), S1(j)  lets warpgroup 0
+// run its softmax on S0(j) while the tensor core works on PV1(j-1) and S1(j),
+// and vice versa (ping-pong of the two Q tiles).
+//
+// Numerics follow the reference (csrc/include/afa_softmax.cuh:12-127,
+// afa_forward_kernel.cuh:83-184): exp2 with log2(e) folded into the scale,
+// the row sum l accumulated from fp32 P before P is rounded to the input type
+// for the PV product, fp32 accumulation, final O / l in fp32.
+//
+// Every mbarrier wait is bounded (globaltimer deadline): on expiry the kernel
+// records AFA_DEV_TIMEOUT_BASE + site in the status word, raises a CTA-wide
+// abort flag and every role returns, so a bug cannot hang the GPU.
+#pragma once
+
+#include <cstdint>
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+
+#include "sm100_ptx.cuh"
+
+#ifndef AFA_DEV_TIMEOUT_BASE
+#define AFA_DEV_TIMEOUT_BASE 0x100
+#endif
+
+namespace afa100 {
+
+// Kernel parameters (passed as __grid_constant__).  Built by the host
+// launcher in afa_fwd_sm100.cu; replaces AFAForwardParams
+// (csrc/include/afa_config.cuh:7-34).
+struct FwdParams {
+  // 4-D tensor maps, dims ordered by increasing stride: (head_dim, seq, head,
+  // batch) when bit t of seq_inner_mask is set, else (head_dim, head, seq,
+  // batch).  Box: 64 head_dim elements (128 bytes) x 128 rows, SWIZZLE_128B.
+  CUtensorMap tm_q;
+  CUtensorMap tm_k;
+  CUtensorMap tm_v;
+  unsigned seq_inner_mask;  // bit 0: q, bit 1: k, bit 2: v
+  void* o;
+  long long o_sb, o_sn, o_sh;  // element strides of O (head_dim stride is 1)
+  int seq_len;
+  int n_heads;
+  int n_q_pairs;  // ceil(seq_len / 256)
+  int n_kv;       // ceil(seq_len / 128)
+  int n_work;     // batch * n_heads * n_q_pairs
+  float scale_log2;  // scale * log2(e)
+  int* status;
+  unsigned long long timeout_ns;
+};
+
+// Bounded-wait sites, reported as AFA_DEV_TIMEOUT_BASE + site.
+enum WaitSite : int {
+  kSiteLoadQEmpty = 1,
+  kSiteLoadKVEmpty = 2,
+  kSiteMmaQFull = 3,
+  kSiteMmaKFull = 4,
+  kSiteMmaVFull = 5,
+  kSiteMmaP0 = 6,
+  kSiteMmaP1 = 7,
+  kSiteSoftmaxS = 8,
+  kSiteSoftmaxO = 9,
+  kSiteMmaDrain = 10,
+};
+
+// Compile-time layout of one kernel instance.
+template <int kD, bool kBF16, int kStages>
+struct FwdLayout {
+  static_assert(kD == 64 || kD == 128, "head_dim must be 64 or 128");
+  static constexpr int kBM = 128;  // query rows per Q tile (= TMEM lanes)
+  static constexpr int kBN = 128;  // key/value rows per K/V tile
+  static constexpr int kAtoms = kD / 64;               // 128-byte swizzle atoms along head_dim
+  static constexpr uint32_t kAtomBytes = 128u * 128u;  // one TMA box: 128 rows x 128 bytes
+  static constexpr uint32_t kTileBytes = kAtoms * kAtomBytes;
+  static constexpr uint32_t kOffQ = 0;  // Q0, Q1
+  static constexpr uint32_t kOffKV = 2 * kTileBytes;
+  static constexpr uint32_t kOffBar = kOffKV + kStages * kTileBytes;
+  // mbarrier indices
+  static constexpr int kBarQFull = 0;
+  static constexpr int kBarQEmpty = 1;
+  static constexpr int kBarKVFull = 2;                   // [kStages]
+  static constexpr int kBarKVEmpty = 2 + kStages;        // [kStages]
+  static constexpr int kBarSFull = 2 + 2 * kStages;      // [2]
+  static constexpr int kBarPReady = kBarSFull + 2;       // [2]
+  static constexpr int kBarOFinal = kBarPReady + 2;      // [2]
+  static constexpr int kBarMmaDrain = kBarOFinal + 2;
+  static constexpr int kNumBars = kBarMmaDrain + 1;
+  static constexpr uint32_t kOffTmemSlot = kOffBar + kNumBars * 8;
+  static constexpr uint32_t kOffAbort = kOffTmemSlot + 4;
+  static constexpr uint32_t kSmemUsed = kOffAbort + 4;
+  static constexpr uint32_t kSmemBytes = kSmemUsed + 1024;  // slack for 1024-byte alignment
+  static constexpr int kThreads = 384;
+  static constexpr int kSoftmaxThreads = 128;
+  static constexpr uint32_t kTmemCols = 512;
+  static constexpr uint32_t kColO = 256;  // O0 at 256, O1 at 256 + kD
+  // Register split: launched at kLaunchRegs per thread (384 threads, 1 CTA/SM);
+  // the producer warpgroup drops to kProducerRegs, the two softmax warpgroups
+  // rise to kSoftmaxRegs.  128 * (72 + 216 + 216) == 384 * 168.
+  static constexpr int kLaunchRegs = 168;
+  static constexpr int kProducerRegs = 72;
+  static constexpr int kSoftmaxRegs = 216;
+  static_assert(kProducerRegs + 2 * kSoftmaxRegs <= 3 * kLaunchRegs, "register split too large");
+  static_assert(kSmemBytes <= 232448, "shared memory budget exceeded");
+};
+
+// Bounded mbarrier waits shared by all roles of a CTA.
+struct CtaSync {
+  volatile int* abort_flag;
+  int* status;
+  unsigned long long timeout_ns;
+
+  __device__ __forceinline__ bool wait(uint32_t bar, uint32_t parity, int site) const {
+    if (mbar_try_wait(bar, parity)) return true;
+    return wait_slow(bar, parity, site, true);
+  }
+
+  // honour_abort = false is used by teardown drains, which must run to the end.
+  __device__ __forceinline__ bool wait_slow(uint32_t bar, uint32_t parity, int site,
+                                         bool honour_abort) const {
+    const uint64_t t0 = globaltimer_ns();
+    for (uint32_t it = 1;; ++it) {
+      if (mbar_try_wait(bar, parity)) return true;
+      if ((it & 127u) == 0u) {
+        if (honour_abort && *abort_flag) return false;
+        const uint64_t dt = globaltimer_ns() - t0;
+        if (dt > timeout_ns || it > (1u << 30)) {
+          *abort_flag = 1;
+          if (status != nullptr) atomicCAS(status, 0, AFA_DEV_TIMEOUT_BASE + site);
+          return false;
+        }
+      }
+    }
+  }
+};
+
+template <bool kBF16>
+__device__ __forceinline__ uint32_t pack2(float lo, float hi) {
+  if constexpr (kBF16) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  } else {
+    __half2 v = __floats2half2_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&v);
+  }
+}
+
+__device__ __forceinline__ void decode_work(int w, int n_q_pairs, int n_heads, int& qp, int& h,
+                                            int& b) {
+  qp = w % n_q_pairs;
+  const int bh = w / n_q_pairs;
+  h = bh % n_heads;
+  b = bh / n_heads;
+}
+
+// ---------------------------------------------------------------------------
+// Role: TMA producer (one thread)
+// ---------------------------------------------------------------------------
+template <int kD, bool kBF16, int kStages>
+__device__ __forceinline__ void role_load(const FwdParams& p, uint32_t sbase, uint32_t bar0,
+                                          const CtaSync& sy) {
+  using L = FwdLayout<kD, kBF16, kStages>;
+  auto bar = [&](int i) { return bar0 + 8u * static_cast<uint32_t>(i); };
+  const uint64_t pol_kv = l2_policy_evict_last();
+  const uint64_t pol_q = l2_policy_evict_first();
+  uint32_t kv_cnt = 0;
+  uint32_t it = 0;
+  for (int w = blockIdx.x; w < p.n_work; w += gridDim.x, ++it) {
+    int qp, h, b;
+    decode_work(w, p.n_q_pairs, p.n_heads, qp, h, b);
+    if (!sy.wait(bar(L::kBarQEmpty), (it & 1u) ^ 1u, kSiteLoadQEmpty)) return;
+    mbar_arrive_expect_tx(bar(L::kBarQFull), 2u * L::kTileBytes);
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+#pragma unroll
+      for (int a = 0; a < L::kAtoms; ++a) {
+        const int row0 = qp * 256 + t * 128;
+        const bool si = (p.seq_inner_mask & 1u) != 0u;
+        tma_load_4d(sbase + L::kOffQ + t * L::kTileBytes + a * L::kAtomBytes, &p.tm_q,
+                    bar(L::kBarQFull), a * 64, si ? row0 : h, si ? h : row0, b, pol_q);
+      }
+    }
+    for (int j = 0; j < p.n_kv; ++j) {
+#pragma unroll
+      for (int kv = 0; kv < 2; ++kv) {
+        const uint32_t slot = kv_cnt % kStages;
+        const uint32_t ph = (kv_cnt / kStages) & 1u;
+        if (!sy.wait(bar(L::kBarKVEmpty + slot), ph ^ 1u, kSiteLoadKVEmpty)) return;
+        mbar_arrive_expect_tx(bar(L::kBarKVFull + slot), L::kTileBytes);
+        const CUtensorMap* map = kv ? &p.tm_v : &p.tm_k;
+        const bool si = (p.seq_inner_mask & (kv ? 4u : 2u)) != 0u;
+        const int row0 = j * 128;
+#pragma unroll
+        for (int a = 0; a < L::kAtoms; ++a) {
+          tma_load_4d(sbase + L::kOffKV + slot * L::kTileBytes + a * L::kAtomBytes, map,
+                      bar(L::kBarKVFull + slot), a * 64, si ? row0 : h, si ? h : row0, b, pol_kv);
+        }
+        ++kv_cnt;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Role: MMA issuer (one thread)
+// ---------------------------------------------------------------------------
+template <int kD, bool kBF16, int kStages>
+__device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t q_addr, uint32_t k_addr) {
+  using L = FwdLayout<kD, kBF16, kStages>;
+  constexpr uint32_t kIdesc = idesc_f16_f32(128, 128, kBF16, false);
+#pragma unroll
+  for (int k = 0; k < kD / 16; ++k) {
+    // K-major SW128: 16-element (32-byte) steps inside a 64-element atom,
+    // then the next atom (next TMA box) for head_dim >= 64.
+    const uint32_t off = (k / 4) * L::kAtomBytes + (k % 4) * 32u;
+    umma_f16_ss(d_tmem, sdesc_lo(q_addr + off, 16), sdesc_lo(k_addr + off, 16), kIdesc,
+                k > 0 ? 1u : 0u);
+  }
+}
+
+template <int kD, bool kBF16, int kStages>
+__device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint32_t v_addr,
+                                         bool accumulate) {
+  using L = FwdLayout<kD, kBF16, kStages>;
+  constexpr uint32_t kIdesc = idesc_f16_f32(128, kD, kBF16, true);
+#pragma unroll
+  for (int k = 0; k < L::kBN / 16; ++k) {
+    // V is MN-major (head_dim contiguous): 8-row groups 1024 B apart (SBO),
+    // 64-element head_dim atoms one TMA box apart (LBO); 16 key rows per step.
+    // P in TMEM: 16 elements of 16 bit = 8 columns per K step.
+    umma_f16_ts(d_tmem, p_tmem + k * 8u, sdesc_lo(v_addr + k * 16u * 128u, L::kAtomBytes), kIdesc,
+                (accumulate || k > 0) ? 1u : 0u);
+  }
+}
+
+template <int kD, bool kBF16, int kStages>
+__device__ __forceinline__ void role_mma(const FwdParams& p, uint32_t sbase, uint32_t bar0,
+                                         uint32_t tmem, const CtaSync& sy) {
+  using L = FwdLayout<kD, kBF16, kStages>;
+  auto bar = [&](int i) { return bar0 + 8u * static_cast<uint32_t>(i); };
+  auto slot_addr = [&](uint32_t s) { return sbase + L::kOffKV + s * L::kTileBytes; };
+  const uint32_t tS0 = tmem + 0u, tS1 = tmem + 128u;
+  const uint32_t tO0 = tmem + L::kColO, tO1 = tmem + L::kColO + kD;
+  const uint32_t q0 = sbase + L::kOffQ, q1 = q0 + L::kTileBytes;
+  uint32_t kv_cnt = 0, it = 0, pph0 = 0, pph1 = 0;
+  bool ok = true;
+  for (int w = blockIdx.x; w < p.n_work && ok; w += gridDim.x, ++it) {
+    if (!sy.wait(bar(L::kBarQFull), it & 1u, kSiteMmaQFull)) { ok = false; break; }
+    uint32_t ks = kv_cnt % kStages;
+    if (!sy.wait(bar(L::kBarKVFull + ks), (kv_cnt / kStages) & 1u, kSiteMmaKFull)) { ok = false; break; }
+    tc_fence_after_sync();
+    issue_qk<kD, kBF16, kStages>(tS0, q0, slot_addr(ks));
+    umma_commit(bar(L::kBarSFull + 0));
+    issue_qk<kD, kBF16, kStages>(tS1, q1, slot_addr(ks));
+    umma_commit(bar(L::kBarSFull + 1));
+    umma_commit(bar(L::kBarKVEmpty + ks));
+    ++kv_cnt;
+    uint32_t vcnt = kv_cnt++;
+    for (int j = 1; j < p.n_kv; ++j) {
+      ks = kv_cnt % kStages;
+      const uint32_t vs = vcnt % kStages;
+      if (!sy.wait(bar(L::kBarKVFull + vs), (vcnt / kStages) & 1u, kSiteMmaVFull)) { ok = false; break; }
+      if (!sy.wait(bar(L::kBarKVFull + ks), (kv_cnt / kStages) & 1u, kSiteMmaKFull)) { ok = false; break; }
+      if (!sy.wait(bar(L::kBarPReady + 0), pph0, kSiteMmaP0)) { ok = false; break; }
+      pph0 ^= 1u;
+      tc_fence_after_sync();
+      issue_pv<kD, kBF16, kStages>(tO0, tS0, slot_addr(vs), j > 1);
+      issue_qk<kD, kBF16, kStages>(tS0, q0, slot_addr(ks));
+      umma_commit(bar(L::kBarSFull + 0));
+      if (!sy.wait(bar(L::kBarPReady + 1), pph1, kSiteMmaP1)) { ok = false; break; }
+      pph1 ^= 1u;
+      tc_fence_after_sync();
+      issue_pv<kD, kBF16, kStages>(tO1, tS1, slot_addr(vs), j > 1);
+      umma_commit(bar(L::kBarKVEmpty + vs));
+      issue_qk<kD, kBF16, kStages>(tS1, q1, slot_addr(ks));
+      umma_commit(bar(L::kBarSFull + 1));
+      umma_commit(bar(L::kBarKVEmpty + ks));
+      ++kv_cnt;
+      vcnt = kv_cnt++;
+    }
+    if (!ok) break;
+    umma_commit(bar(L::kBarQEmpty));  // all S MMAs of this work item issued: Q may be reloaded
+    const uint32_t vs = vcnt % kStages;
+    if (!sy.wait(bar(L::kBarKVFull + vs), (vcnt / kStages) & 1u, kSiteMmaVFull)) { ok = false; break; }
+    if (!sy.wait(bar(L::kBarPReady + 0), pph0, kSiteMmaP0)) { ok = false; break; }
+    pph0 ^= 1u;
+    tc_fence_after_sync();
+    issue_pv<kD, kBF16, kStages>(tO0, tS0, slot_addr(vs), p.n_kv > 1);
+    umma_commit(bar(L::kBarOFinal + 0));
+    if (!sy.wait(bar(L::kBarPReady + 1), pph1, kSiteMmaP1)) { ok = false; break; }
+    pph1 ^= 1u;
+    tc_fence_after_sync();
+    issue_pv<kD, kBF16, kStages>(tO1, tS1, slot_addr(vs), p.n_kv > 1);
+    umma_commit(bar(L::kBarOFinal + 1));
+    umma_commit(bar(L::kBarKVEmpty + vs));
+  }
+  // Drain: every MMA issued by this thread has completed before teardown
+  // releases tensor memory.
+  umma_commit(bar(L::kBarMmaDrain));
+  if (!mbar_try_wait(bar(L::kBarMmaDrain), 0)) sy.wait_slow(bar(L::kBarMmaDrain), 0, kSiteMmaDrain, false);
+}
+
+// ---------------------------------------------------------------------------
+// Role: softmax + correction + epilogue (one warpgroup per Q tile)
+// ---------------------------------------------------------------------------
+template <int kD, bool kBF16, int kStages>
+__device__ __forceinline__ void role_softmax(const FwdParams& p, int wg, uint32_t bar0,
+                                             uint32_t tmem, const CtaSync& sy) {
+  using L = FwdLayout<kD, kBF16, kStages>;
+  using T = typename std::conditional<kBF16, __nv_bfloat16, __half>::type;
+  auto bar = [&](int i) { return bar0 + 8u * static_cast<uint32_t>(i); };
+  const int warp_in_wg = (threadIdx.x >> 5) & 3;
+  const int row = warp_in_wg * 32 + static_cast<int>(threadIdx.x & 31);
+  const uint32_t lane_field = static_cast<uint32_t>(warp_in_wg * 32) << 16;
+  const uint32_t tS = tmem + lane_field + static_cast<uint32_t>(wg) * 128u;
+  const uint32_t tO = tmem + lane_field + L::kColO + static_cast<uint32_t>(wg) * kD;
+  const float sl2 = p.scale_log2;
+  const uint32_t bar_s = bar(L::kBarSFull + wg);
+  const uint32_t bar_p = bar(L::kBarPReady + wg);
+  const uint32_t bar_o = bar(L::kBarOFinal + wg);
+  uint32_t sph = 0, oph = 0;
+
+  for (int w = blockIdx.x; w < p.n_work; w += gridDim.x) {
+    int qp, h, b;
+    decode_work(w, p.n_q_pairs, p.n_heads, qp, h, b);
+    const int q_row = qp * 256 + wg * 128 + row;
+    float m_ref = -INFINITY;  // running reference max, already in log2 units (x scale*log2e)
+    float l = 0.f;
+    for (int j = 0; j < p.n_kv; ++j) {
+      if (!sy.wait(bar_s, sph, kSiteSoftmaxS)) return;
+      sph ^= 1u;
+      tc_fence_after_sync();
+      uint32_t sr[128];
+      tmem_ld64_sync(tS, *reinterpret_cast<uint32_t(*)[64]>(&sr[0]));
+      tmem_ld64_sync(tS + 64u, *reinterpret_cast<uint32_t(*)[64]>(&sr[64]));
+      float s[128];
+#pragma unroll
+      for (int k = 0; k < 128; ++k) s[k] = __uint_as_float(sr[k]);
+      const int valid = p.seq_len - j * 128;  // key columns of this tile inside the sequence
+      if (valid < 128) {
+#pragma unroll
+        for (int k = 0; k < 128; ++k) s[k] = (k < valid) ? s[k] : -INFINITY;
+      }
+      float mx0 = s[0], mx1 = s[1], mx2 = s[2], mx3 = s[3];
+#pragma unroll
+      for (int k = 4; k < 128; k += 4) {
+        mx0 = fmaxf(mx0, s[k]);
+        mx1 = fmaxf(mx1, s[k + 1]);
+        mx2 = fmaxf(mx2, s[k + 2]);
+        mx3 = fmaxf(mx3, s[k + 3]);
+      }
+      const float m_new = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sl2;
+      const bool need = m_new > m_ref + 8.0f;
+      // alpha rescales the running sum and O from the old reference max.
+      const float alpha = need ? ex2_approx(m_ref - m_new) : 1.0f;
+      if (need) m_ref = m_new;
+      uint32_t pk[64];
+      float ls0 = 0.f, ls1 = 0.f;
+#pragma unroll
+      for (int k = 0; k < 128; k += 2) {
+        const float p0 = ex2_approx(fmaf(s[k], sl2, -m_ref));
+        const float p1 = ex2_approx(fmaf(s[k + 1], sl2, -m_ref));
+        ls0 += p0;
+        ls1 += p1;
+        pk[k >> 1] = pack2<kBF16>(p0, p1);
+      }
+      l = l * alpha + (ls0 + ls1);
+      tmem_st32(tS, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
+      tmem_st32(tS + 32u, *reinterpret_cast<uint32_t(*)[32]>(&pk[32]));
+      if (j > 0 && __any_sync(0xffffffffu, need)) {
+        // Conditional rescale of O.  The previous PV of this tile has
+        // completed (it was committed before S(j)), and the next one waits for
+        // this warpgroup's p_ready: O is quiescent here.
+#pragma unroll
+        for (int c = 0; c < kD / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32_sync(tO + c * 32u, o);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+          tmem_st32(tO + c * 32u, o);
+        }
+      }
+      tmem_wait_st();
+      tc_fence_before_sync();
+      mbar_arrive(bar_p);
+    }
+    // Epilogue: O / l, round to the input type, store the row.
+    if (!sy.wait(bar_o, oph, kSiteSoftmaxO)) return;
+    oph ^= 1u;
+    tc_fence_after_sync();
+    const float inv_l = 1.0f / l;
+    const bool row_ok = q_row < p.seq_len;
+    T* orow = static_cast<T*>(p.o) + static_cast<long long>(b) * p.o_sb +
+              static_cast<long long>(q_row) * p.o_sn + static_cast<long long>(h) * p.o_sh;
+#pragma unroll
+    for (int c = 0; c < kD / 32; ++c) {
+      uint32_t o[32];
+      tmem_ld32_sync(tO + c * 32u, o);
+      uint32_t pk[16];
+#pragma unroll
+      for (int e = 0; e < 16; ++e)
+        pk[e] = pack2<kBF16>(__uint_as_float(o[2 * e]) * inv_l, __uint_as_float(o[2 * e + 1]) * inv_l);
+      if (row_ok) {
+#pragma unroll
+        for (int v4 = 0; v4 < 4; ++v4)
+          st_global_v4(orow + c * 32 + v4 * 8, pk[4 * v4], pk[4 * v4 + 1], pk[4 * v4 + 2],
+                       pk[4 * v4 + 3]);
+      }
+    }
+    tc_fence_before_sync();
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Kernel
+// ---------------------------------------------------------------------------
+template <int kD, bool kBF16, int kStages>
+__global__ void __launch_bounds__(384, 1) afa_fwd_sm100_kernel(const __grid_constant__ FwdParams p) {
+  using L = FwdLayout<kD, kBF16, kStages>;
+  extern __shared__ __align__(1024) uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t sbase = (raw + 1023u) & ~1023u;
+  uint8_t* smem = smem_raw + (sbase - raw);
+  const uint32_t bar0 = sbase + L::kOffBar;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kOffTmemSlot);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kOffAbort);
+
+  const int warp = __shfl_sync(0xffffffffu, static_cast<int>(threadIdx.x >> 5), 0);
+  const uint32_t lane = threadIdx.x & 31u;
+
+  if (warp == 0 && lane == 0) {
+    for (int i = 0; i < L::kNumBars; ++i) {
+      const uint32_t count = (i == L::kBarPReady || i == L::kBarPReady + 1) ? L::kSoftmaxThreads : 1u;
+      mbar_init(bar0 + 8u * i, count);
+    }
+    *abort_flag = 0;
+    fence_mbarrier_init();
+    tma_prefetch_desc(&p.tm_q);
+    tma_prefetch_desc(&p.tm_k);
+    tma_prefetch_desc(&p.tm_v);
+  }
+  if (warp == 2) {
+    tmem_alloc(smem_u32(tmem_slot), L::kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before_sync();
+  __syncthreads();
+  tc_fence_after_sync();
+  const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
+  const CtaSync sy{abort_flag, p.status, p.timeout_ns};
+
+  if (warp < 4) {
+    setmaxnreg_dec<L::kProducerRegs>();
+    if (warp == 0) {
+      if (lane == 0) role_load<kD, kBF16, kStages>(p, sbase, bar0, sy);
+    } else if (warp == 1) {
+      if (lane == 0) role_mma<kD, kBF16, kStages>(p, sbase, bar0, tmem, sy);
+    }
+  } else {
+    setmaxnreg_inc<L::kSoftmaxRegs>();
+    role_softmax<kD, kBF16, kStages>(p, (warp - 4) >> 2, bar0, tmem, sy);
+  }
+
+  tc_fence_before_sync();
+  __syncthreads();
+  if (warp == 2) {
+    tc_fence_after_sync();
+    tmem_dealloc(tmem, L::kTmemCols);
+  }
+}
+
+}  // namespace afa100

@@ -1,0 +1,217 @@
+// afa_torch_binding.cpp -- the `afa_flash_attention_kernels` torch extension.
+//
+// Same Python surface as the reference binding
+// (csrc/ampere_flash_attention.cu:138-151):
+//     O, ms = afa_flash_attention_kernels.forward(kernel_cfg, q, k, v, o, benchmark=False)
+// with the same checks and RuntimeError messages where the behaviour carries
+// over (csrc/ampere_flash_attention.cu:39-99).  Underneath it calls the C ABI
+// afa_fwd_sm100() (include/afa_sm100.h); this file holds no device code.
+//
+// Deliberate differences from the reference binding:
+//   * the device must be compute capability 10.0 (the kernel is sm_100a code);
+//   * the kernel table is keyed on (dtype, d_head) -- the Ampere tiling knobs
+//     of the config are accepted and ignored;
+//   * any seq_len >= 1 is accepted (no B_r/B_c divisibility rule) and inputs
+//     may be strided views as long as head_dim is contiguous and the other
+//     strides are multiples of 8 elements;
+//   * `o` is checked against q's shape (the reference compared q with v);
+//   * with benchmark=False the returned runtime is 0.0 (the reference returned
+//     an uninitialised float); with benchmark=True the events are destroyed
+//     and the device status word is checked.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cuda_runtime.h>
+#include <torch/extension.h>
+
+#include <mutex>
+#include <optional>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "afa_sm100.h"
+
+namespace {
+
+#define AFA_CHECK_CUDA(x) TORCH_CHECK((x).device().is_cuda(), #x " must be a CUDA tensor")
+#define AFA_CHECK_LAST_DIM(x) \
+  TORCH_CHECK((x).dim() == 4 && (x).stride(3) == 1, #x " must be 4-D [batch, seq, heads, head_dim] with a contiguous head_dim")
+
+// The key fields of the Python AFAForwardKernelConfig.  All 13 attributes are
+// read, as in py_to_cpp_kernel_config (csrc/ampere_flash_attention.cu:16-33),
+// so a malformed config object fails the same way.
+struct KernelKey {
+  int dtype;
+  int d_head;
+};
+
+KernelKey py_to_cpp_kernel_config(const py::object& cfg) {
+  KernelKey key{py::cast<int>(cfg.attr("dtype")), py::cast<int>(cfg.attr("d_head"))};
+  static const char* kInts[] = {"B_r", "B_c", "n_warps", "Q_col_fragments_per_warp_gemm",
+                                "K_col_fragments_per_warp_gemm", "V_col_fragments_per_warp_gemm"};
+  static const char* kBools[] = {"async_copy", "eager_load_blocks", "swizzled",
+                                 "mma_double_buffer_loads", "optimized_softmax"};
+  for (const char* a : kInts) (void)py::cast<int>(cfg.attr(a));
+  for (const char* a : kBools) (void)py::cast<bool>(cfg.attr(a));
+  return key;
+}
+
+int dtype_code(const at::Tensor& t) {
+  if (t.scalar_type() == at::kHalf) return AFA_DTYPE_FP16;
+  if (t.scalar_type() == at::kBFloat16) return AFA_DTYPE_BF16;
+  return -1;
+}
+
+// One persistent device status word per device (int32, zero = ok).
+std::mutex g_status_mu;
+std::vector<at::Tensor> g_status;
+
+at::Tensor& status_word(const at::Device& dev) {
+  std::lock_guard<std::mutex> lock(g_status_mu);
+  const size_t i = static_cast<size_t>(dev.index());
+  if (g_status.size() <= i) g_status.resize(i + 1);
+  if (!g_status[i].defined())
+    g_status[i] = at::zeros({1}, at::TensorOptions().dtype(at::kInt).device(dev));
+  return g_status[i];
+}
+
+int32_t read_and_clear_status(const at::Device& dev) {
+  at::Tensor& s = status_word(dev);
+  const int32_t v = s.item<int32_t>();
+  if (v != 0) s.zero_();
+  return v;
+}
+
+std::tuple<at::Tensor, double> flash_attention_forward(const py::object& py_cfg,
+                                                       const at::Tensor& TQ, const at::Tensor& TK,
+                                                       const at::Tensor& TV,
+                                                       std::optional<at::Tensor> out_,
+                                                       bool benchmark) {
+  AFA_CHECK_CUDA(TQ);
+  AFA_CHECK_CUDA(TK);
+  AFA_CHECK_CUDA(TV);
+  AFA_CHECK_LAST_DIM(TQ);
+  AFA_CHECK_LAST_DIM(TK);
+  AFA_CHECK_LAST_DIM(TV);
+
+  c10::cuda::CUDAGuard device_guard{TQ.device()};
+  const int dev = TQ.device().index();
+  int major = 0, minor = 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+  TORCH_CHECK(major == 10 && minor == 0,
+              "Flash Attention (sm_100a build) requires SM_100 (current: SM_", major, ".", minor,
+              ")");
+
+  const int dt = dtype_code(TQ);
+  TORCH_CHECK(dt > 0, "Only fp16 and bf16 are supported");
+  TORCH_CHECK(TK.dtype() == TQ.dtype(), "Input tensors must have the same data type");
+  TORCH_CHECK(TV.dtype() == TQ.dtype(), "Input tensors must have the same data type");
+  TORCH_CHECK(TK.device() == TQ.device() && TV.device() == TQ.device(),
+              "Input tensors must be on the same device");
+
+  const KernelKey cfg = py_to_cpp_kernel_config(py_cfg);
+  TORCH_CHECK(afa_fwd_sm100_supported(cfg.dtype, cfg.d_head) == 1,
+              "Kernel configuration was not found: no sm_100a kernel for dtype code ", cfg.dtype,
+              ", d_head ", cfg.d_head);
+  TORCH_CHECK(cfg.dtype == dt, "Kernel configuration dtype does not match input dtype");
+  TORCH_CHECK(cfg.d_head == TQ.size(3), "Kernel configuration d_head (", cfg.d_head,
+              ") does not match the input head_dim (", TQ.size(3), ")");
+
+  TORCH_CHECK(TQ.sizes() == TK.sizes(), "Query and key tensors have same shape");
+  TORCH_CHECK(TQ.sizes() == TV.sizes(), "Query and value tensors have same shape");
+  TORCH_CHECK(TQ.size(0) > 0 && TQ.size(1) > 0 && TQ.size(2) > 0,
+              "batch, seq_len and n_heads must be positive");
+  TORCH_CHECK(TQ.size(0) <= INT32_MAX && TQ.size(1) <= INT32_MAX && TQ.size(2) <= INT32_MAX,
+              "tensor dimension too large");
+
+  at::Tensor TO;
+  if (out_.has_value() && out_->defined()) {
+    TO = out_.value();
+    AFA_CHECK_CUDA(TO);
+    AFA_CHECK_LAST_DIM(TO);
+    TORCH_CHECK(TO.dtype() == TQ.dtype(), "Output tensor must have the same dtype as inputs");
+    TORCH_CHECK(TQ.sizes() == TO.sizes(), "Query and output tensors have same shape");
+    TORCH_CHECK(TO.device() == TQ.device(), "Output tensor must be on the same device");
+  } else {
+    TO = at::empty_like(TQ, at::MemoryFormat::Contiguous);
+  }
+
+  AfaFwdArgs args{};
+  args.q = TQ.data_ptr();
+  args.k = TK.data_ptr();
+  args.v = TV.data_ptr();
+  args.o = TO.data_ptr();
+  const at::Tensor* ts[4] = {&TQ, &TK, &TV, &TO};
+  int64_t* ss[4] = {args.q_strides, args.k_strides, args.v_strides, args.o_strides};
+  for (int t = 0; t < 4; ++t)
+    for (int d = 0; d < 3; ++d) ss[t][d] = ts[t]->stride(d);
+  args.batch = static_cast<int32_t>(TQ.size(0));
+  args.seq_len = static_cast<int32_t>(TQ.size(1));
+  args.n_heads = static_cast<int32_t>(TQ.size(2));
+  args.head_dim = static_cast<int32_t>(TQ.size(3));
+  args.dtype = dt;
+  args.scale = 0.f;  // 1/sqrt(d_head), fixed as in the reference kernel
+  at::Tensor& status = status_word(TQ.device());
+  args.status = status.data_ptr<int32_t>();
+  args.timeout_ns = 0;
+
+  cudaStream_t stream = at::cuda::getCurrentCUDAStream().stream();
+  float runtime = 0.f;
+  cudaEvent_t start = nullptr, stop = nullptr;
+  if (benchmark) {
+    TORCH_CHECK(cudaEventCreate(&start) == cudaSuccess && cudaEventCreate(&stop) == cudaSuccess,
+                "cudaEventCreate failed");
+    cudaEventRecord(start, stream);
+  }
+  const int rc = afa_fwd_sm100(&args, stream);
+  if (benchmark) {
+    cudaEventRecord(stop, stream);
+    cudaEventSynchronize(stop);
+    cudaEventElapsedTime(&runtime, start, stop);
+    cudaEventDestroy(start);
+    cudaEventDestroy(stop);
+  }
+  TORCH_CHECK(rc == AFA_OK, "afa_fwd_sm100 failed: ", afa_strerror(rc));
+  if (benchmark) {
+    const int32_t st = read_and_clear_status(TQ.device());
+    TORCH_CHECK(st == 0, "attention kernel reported: ", afa_status_string(st));
+  }
+  return std::make_tuple(TO, static_cast<double>(runtime));
+}
+
+// Reads (and clears) the device status word of `device`; raises RuntimeError
+// if a kernel since the last check reported an error.  Synchronises.
+void check_status(int64_t device) {
+  const at::Device dev(at::kCUDA, static_cast<c10::DeviceIndex>(device));
+  c10::cuda::CUDAGuard g{dev};
+  const int32_t st = read_and_clear_status(dev);
+  TORCH_CHECK(st == 0, "attention kernel reported: ", afa_status_string(st));
+}
+
+std::vector<std::tuple<int, int>> kernel_keys() {
+  std::vector<std::tuple<int, int>> out;
+  for (int dt : {AFA_DTYPE_FP16, AFA_DTYPE_BF16})
+    for (int d : {64, 128})
+      if (afa_fwd_sm100_supported(dt, d)) out.emplace_back(dt, d);
+  return out;
+}
+
+// Raises a RuntimeError whose message is formatted from integers -- the same
+// error path as the shape/config checks above; lets the CPU tests verify that
+// C++ exceptions cross the binding intact.
+void raise_formatted_error(int64_t a, int64_t b) {
+  TORCH_CHECK(false, "formatted error ", a, " / ", b);
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.def("forward", &flash_attention_forward, py::arg("kernel_cfg"), py::arg("q"), py::arg("k"),
+        py::arg("v"), py::arg("o") = py::none(), py::arg("benchmark") = false,
+        "Flash Attention forward (CUDA, sm_100a)");
+  m.def("check_status", &check_status, py::arg("device") = 0,
+        "Raise RuntimeError if a kernel on `device` reported an error since the last check");
+  m.def("_raise_formatted_error", &raise_formatted_error, py::arg("a"), py::arg("b"));
+  m.def("kernel_keys", &kernel_keys, "(dtype code, d_head) pairs with a compiled sm_100a kernel");
+}

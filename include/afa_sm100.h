@@ -1,0 +1,103 @@
+/*
+ * afa_sm100.h -- C ABI of the B200 (sm_100a) attention-forward library
+ * (libafa_sm100.so).
+ *
+ * Computes the non-causal attention forward  O = softmax(Q K^T * scale) V  for
+ * fp16/bf16 tensors laid out as [batch, seq_len, n_heads, head_dim], the same
+ * operation and layout as the reference's torch binding
+ * `afa_flash_attention_kernels.forward` (csrc/ampere_flash_attention.cu:35-136).
+ *
+ * Plain C types only: pointers are device addresses, the stream is a
+ * cudaStream_t passed as void*.  No call allocates, frees or synchronizes; all
+ * buffers belong to the caller.  Every entry point returns an AFA_* status code
+ * and never throws.
+ */
+#ifndef AFA_SM100_H_
+#define AFA_SM100_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Element types: the integer values of torch's ScalarType, as used by the
+ * reference's Python DType enum (afa_py/afa_config.py:8-28: FP16 = 5, BF16 = 15). */
+#define AFA_DTYPE_FP16 5
+#define AFA_DTYPE_BF16 15
+
+/* Return codes. */
+#define AFA_OK 0
+#define AFA_ERR_INVALID_ARGUMENT 1   /* null pointer, non-positive size, bad stride */
+#define AFA_ERR_UNSUPPORTED_DTYPE 2  /* dtype not fp16/bf16 */
+#define AFA_ERR_NO_KERNEL 3          /* no compiled kernel for (dtype, head_dim) */
+#define AFA_ERR_MISALIGNED 4         /* base address / stride not 16-byte aligned */
+#define AFA_ERR_NO_DEVICE 5          /* no current CUDA device */
+#define AFA_ERR_ARCH 6               /* device is not compute capability 10.0 */
+#define AFA_ERR_TENSOR_MAP 7         /* cuTensorMapEncodeTiled rejected a tensor */
+#define AFA_ERR_LAUNCH 8             /* kernel launch failed */
+#define AFA_ERR_DEVICE_TIMEOUT 9     /* a device-side bounded wait ran out (status word) */
+#define AFA_ERR_TOO_LARGE 10         /* a size exceeds what the kernel indexes */
+
+/* Arguments of one forward call.  Strides are in elements, for the
+ * (batch, seq, head) dimensions; head_dim must be contiguous (stride 1).
+ * Replaces the reference's AFAForwardParams (csrc/include/afa_config.cuh:7-34),
+ * which had one stride set shared by all four tensors. */
+typedef struct AfaFwdArgs {
+  const void* q;
+  const void* k;
+  const void* v;
+  void* o;
+  int64_t q_strides[3];
+  int64_t k_strides[3];
+  int64_t v_strides[3];
+  int64_t o_strides[3];
+  int32_t batch;
+  int32_t seq_len;
+  int32_t n_heads;
+  int32_t head_dim;   /* 64 or 128 */
+  int32_t dtype;      /* AFA_DTYPE_FP16 or AFA_DTYPE_BF16 */
+  float scale;        /* softmax scale; <= 0 selects 1/sqrt(head_dim) as the reference */
+  int32_t* status;    /* optional device int32: 0 = ok, else an AFA_DEV_* code (see below) */
+  uint64_t timeout_ns; /* bound of every device-side wait; 0 selects the default (4 s) */
+} AfaFwdArgs;
+
+/*
+ * Launch the forward kernel on `stream` (a cudaStream_t) for the current device.
+ * Replaces the launch path of the reference's flash_attention_forward
+ * (csrc/ampere_flash_attention.cu:35-136) and its kernel table lookup
+ * (csrc/include/afa_preset_kernels.cuh:10-54), keyed here on (dtype, head_dim).
+ * Asynchronous: returns after the launch.  Argument errors are reported before
+ * any CUDA call is made.
+ */
+int afa_fwd_sm100(const AfaFwdArgs* args, void* stream);
+
+/* Human-readable text for an AFA_* return code (static storage). */
+const char* afa_strerror(int code);
+
+/*
+ * Device status words written by the kernel into AfaFwdArgs.status (first error
+ * wins).  AFA_DEV_TIMEOUT_BASE + site: a bounded mbarrier wait at `site` ran
+ * out and the kernel returned early (the output is then undefined).
+ * Decodes a status word into text (static storage).
+ */
+#define AFA_DEV_OK 0
+#define AFA_DEV_TIMEOUT_BASE 0x100
+const char* afa_status_string(int32_t status);
+
+/* 1 if a kernel is compiled for (dtype, head_dim), else 0.  Host-only. */
+int afa_fwd_sm100_supported(int32_t dtype, int32_t head_dim);
+
+/* Dynamic shared memory bytes and threads per CTA of the (dtype, head_dim)
+ * kernel, or -1 if not compiled.  Host-only. */
+int afa_fwd_sm100_smem_bytes(int32_t dtype, int32_t head_dim);
+int afa_fwd_sm100_threads(void);
+
+/* Library ABI version (major * 100 + minor). */
+int afa_sm100_version(void);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* AFA_SM100_H_ */
