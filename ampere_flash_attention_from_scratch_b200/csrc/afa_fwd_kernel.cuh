@@ -121,6 +121,17 @@ struct FwdLayout {
   static constexpr int kProducerRegs = 72;
   static constexpr int kSoftmaxRegs = 216;
   static_assert(kProducerRegs + 2 * kSoftmaxRegs <= 3 * kLaunchRegs, "register split too large");
+  // Share of exp2 evaluations moved from the MUFU unit to the FMA pipe: in
+  // every group of 8 consecutive column pairs, the first kEmuPairs use the
+  // polynomial.  At head_dim 128 the MUFU work per K/V tile equals the MMA
+  // work; at 64 it is twice the MMA work.
+#ifndef AFA_EXP_EMU_PAIRS_D128
+#define AFA_EXP_EMU_PAIRS_D128 0
+#endif
+#ifndef AFA_EXP_EMU_PAIRS_D64
+#define AFA_EXP_EMU_PAIRS_D64 0
+#endif
+  static constexpr int kEmuPairs = kD == 128 ? AFA_EXP_EMU_PAIRS_D128 : AFA_EXP_EMU_PAIRS_D64;
   static_assert(kSmemBytes <= 232448, "shared memory budget exceeded");
 };
 
@@ -163,6 +174,32 @@ __device__ __forceinline__ uint32_t pack2(float lo, float hi) {
     __half2 v = __floats2half2_rn(lo, hi);
     return *reinterpret_cast<uint32_t*>(&v);
   }
+}
+
+// 2^x for two values on the FMA/ALU pipes instead of the MUFU unit.
+// Cody-Waite style split x = j + f, j = rint(x) (obtained by adding and
+// subtracting 1.5 * 2^23), |f| <= 1/2; 2^f by a degree-3 polynomial whose
+// coefficients are a relative-error minimax fit on [-1/2, 1/2] made for this
+// kernel (Remez exchange; max relative error 7.2e-5, 1.4e-4 after fp32
+// rounding over x in [-126, 8]); 2^j is added to the exponent field.  Inputs
+// are clamped to >= -126 so the exponent never wraps (2^-126 ~ 1e-38, zero
+// after rounding P to fp16/bf16); inputs never exceed +8 here (conditional
+// rescaling bounds x = s*c - m_ref by 8).
+__device__ __forceinline__ float2 exp2_fma_pipe2(float2 x) {
+  constexpr float kRound = 12582912.0f;  // 1.5 * 2^23
+  constexpr float kC0 = 0.99992806f, kC1 = 0.69326097f, kC2 = 0.24261113f, kC3 = 0.05517167f;
+  x.x = fmaxf(x.x, -126.0f);
+  x.y = fmaxf(x.y, -126.0f);
+  const float2 t = __fadd2_rn(x, make_float2(kRound, kRound));
+  const float2 j = __fadd2_rn(t, make_float2(-kRound, -kRound));
+  const float2 f = __ffma2_rn(j, make_float2(-1.0f, -1.0f), x);
+  float2 q = __ffma2_rn(f, make_float2(kC3, kC3), make_float2(kC2, kC2));
+  q = __ffma2_rn(q, f, make_float2(kC1, kC1));
+  q = __ffma2_rn(q, f, make_float2(kC0, kC0));
+  float2 r;
+  r.x = __int_as_float(__float_as_int(q.x) + (__float_as_int(t.x) << 23));
+  r.y = __int_as_float(__float_as_int(q.y) + (__float_as_int(t.y) << 23));
+  return r;
 }
 
 __device__ __forceinline__ void decode_work(int w, int n_q_pairs, int n_heads, int& qp, int& h,
@@ -361,29 +398,40 @@ __device__ __forceinline__ void role_softmax(const FwdParams& p, int wg, uint32_
 #pragma unroll
         for (int k = 0; k < 128; ++k) s[k] = (k < valid) ? s[k] : -INFINITY;
       }
-      float mx0 = s[0], mx1 = s[1], mx2 = s[2], mx3 = s[3];
+      float mx0 = -INFINITY, mx1 = -INFINITY, mx2 = -INFINITY, mx3 = -INFINITY;
 #pragma unroll
-      for (int k = 4; k < 128; k += 4) {
-        mx0 = fmaxf(mx0, s[k]);
-        mx1 = fmaxf(mx1, s[k + 1]);
-        mx2 = fmaxf(mx2, s[k + 2]);
-        mx3 = fmaxf(mx3, s[k + 3]);
+      for (int k = 0; k < 128; k += 8) {
+        mx0 = fmax3(mx0, s[k], s[k + 1]);
+        mx1 = fmax3(mx1, s[k + 2], s[k + 3]);
+        mx2 = fmax3(mx2, s[k + 4], s[k + 5]);
+        mx3 = fmax3(mx3, s[k + 6], s[k + 7]);
       }
-      const float m_new = fmaxf(fmaxf(mx0, mx1), fmaxf(mx2, mx3)) * sl2;
+      const float m_new = fmaxf(fmax3(mx0, mx1, mx2), mx3) * sl2;
       const bool need = m_new > m_ref + 8.0f;
       // alpha rescales the running sum and O from the old reference max.
       const float alpha = need ? ex2_approx(m_ref - m_new) : 1.0f;
       if (need) m_ref = m_new;
       uint32_t pk[64];
-      float ls0 = 0.f, ls1 = 0.f;
+      const float2 c2 = make_float2(sl2, sl2);
+      const float2 nm2 = make_float2(-m_ref, -m_ref);
+      float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
 #pragma unroll
       for (int k = 0; k < 128; k += 2) {
-        const float p0 = ex2_approx(fmaf(s[k], sl2, -m_ref));
-        const float p1 = ex2_approx(fmaf(s[k + 1], sl2, -m_ref));
-        ls0 += p0;
-        ls1 += p1;
-        pk[k >> 1] = pack2<kBF16>(p0, p1);
+        const float2 x = __ffma2_rn(make_float2(s[k], s[k + 1]), c2, nm2);
+        float2 e;
+        if (((k >> 1) & 7) < L::kEmuPairs) {
+          e = exp2_fma_pipe2(x);
+        } else {
+          e.x = ex2_approx(x.x);
+          e.y = ex2_approx(x.y);
+        }
+        if ((k >> 1) & 1)
+          acc1 = __fadd2_rn(acc1, e);
+        else
+          acc0 = __fadd2_rn(acc0, e);
+        pk[k >> 1] = pack2<kBF16>(e.x, e.y);
       }
+      const float ls0 = acc0.x + acc1.x, ls1 = acc0.y + acc1.y;
       l = l * alpha + (ls0 + ls1);
       tmem_st32(tS, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
       tmem_st32(tS + 32u, *reinterpret_cast<uint32_t(*)[32]>(&pk[32]));

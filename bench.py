@@ -1,0 +1,424 @@
+#!/usr/bin/env python
+"""Benchmark of the sm_100a attention forward (the reference's headline metric).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--config cfg4]
+
+For N > 1 it runs under torchrun, one rank per GPU (RANK / LOCAL_RANK /
+WORLD_SIZE from the environment, NCCL process group).  The workload's batch is
+split evenly over the ranks ([16, 8192, 32, 128] fp16 by default: each rank
+takes 16/N of the 512 (batch, head) slices); there is no collective on the data
+path, only a barrier around the timed region and a MAX all-reduce of the time.
+
+One step = one forward call over the rank's whole shard.  Rank 0 prints ONE
+JSON line on stdout:
+  value       4*B*H*N^2*d over all ranks / max-over-ranks device time (CUDA events,
+              inputs resident in HBM; the 3.2 GB of inputs exceed the 126 MB L2,
+              so no flush is needed between steps)
+  e2e         the same metric through afa_flash_attention_kernels.forward with
+              pinned host inputs copied to the device and O copied back inside
+              every timed step
+  roofline    tensor-core bound: achieved TFLOP/s of the kernel vs the measured
+              dense bf16 peak (MEASURED_PEAKS.json), DRAM traffic from the
+              committed ncu summary
+  cpu_baseline  naive torch fp32 attention on the host cores, on a bounded sample
+              of (batch, head) slices, extrapolated linearly (every slice does the
+              same work)
+  clocks      nvidia-smi samples taken during the timed regions
+
+--impl reference times the reference's CPU path (the naive torch fp32
+attention of the oracle; the reference has no CPU implementation of its own)
+on the host cores of rank 0; other ranks exit without work.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from datetime import timedelta
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+from ampere_flash_attention_from_scratch_b200.workloads import WORKLOADS, Workload, make_inputs  # noqa: E402
+
+METRIC = "attn fwd TFLOP/s (4·B·H·N²·d) & % of B200 dense FP16 peak at [16,N,32,128]"
+NOMINAL_DENSE_TFLOPS = 2250.0
+FALLBACK_PEAK = {"bf16_tflops": 1590.0, "hbm_gbs": 6650.0}
+TRAFFIC_FILE = ROOT / "profiles" / "traffic_per_launch.txt"
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+# ---------------------------------------------------------------------------
+# helpers
+# ---------------------------------------------------------------------------
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            d = json.loads(p.read_text())
+            return d, "measured"
+        except Exception:  # pragma: no cover
+            pass
+    return dict(FALLBACK_PEAK), "fallback"
+
+
+def load_traffic(workload: str):
+    """DRAM bytes per launch of the kernel for `workload`, from the committed ncu summary."""
+    if not TRAFFIC_FILE.exists():
+        return None
+    for line in TRAFFIC_FILE.read_text().splitlines():
+        parts = line.split()
+        if len(parts) >= 2 and parts[0] == workload:
+            try:
+                return int(float(parts[1]))
+            except ValueError:
+                return None
+    return None
+
+
+class ClockSampler:
+    """nvidia-smi -lms sampling of SM clock and throttle reasons for one GPU."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+        self.thread = None
+        self.marks = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+        self.thread = threading.Thread(target=self._read, daemon=True)
+        self.thread.start()
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append((time.time(), line.strip()))
+
+    def mark(self, name):
+        self.marks.append((name, time.time()))
+
+    def stop(self):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+            if self.thread is not None:
+                self.thread.join(timeout=2)
+
+    def summary(self, windows):
+        """Samples that fall inside any of the (t0, t1) windows."""
+        sms, maxs, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for t, line in self.lines:
+            if not any(t0 <= t <= t1 for t0, t1 in windows):
+                continue
+            parts = [x.strip() for x in line.split(",")]
+            if len(parts) < 8:
+                continue
+            try:
+                sms.append(float(parts[0]))
+                maxs.append(float(parts[1]))
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[4:8]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        if not sms:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sms), "sm_max_mhz": max(maxs), "reasons": sorted(reasons), "samples": len(sms)}
+
+
+def cpu_attention_rate(wl: Workload, budget_s: float, max_slices: int = 64):
+    """Naive torch fp32 attention on the host cores over (b, h) slices until the
+    time budget is spent; returns (TFLOP/s, slices, seconds, threads)."""
+    from oracle.attention_oracle import attention_fp32  # the CPU baseline only
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    B, N, H, d = wl.shape
+    g = torch.Generator().manual_seed(0)
+    q = (torch.randn(1, N, 1, d, generator=g) * wl.sigma_qk).to(wl.dtype)
+    k = (torch.randn(1, N, 1, d, generator=g) * wl.sigma_qk).to(wl.dtype)
+    v = torch.randn(1, N, 1, d, generator=g).to(wl.dtype)
+    attention_fp32(q, k, v)  # warm-up (allocator, thread pool)
+    flops_slice = 4 * N * N * d
+    t0 = time.perf_counter()
+    n = 0
+    while n < max_slices:
+        attention_fp32(q, k, v)
+        n += 1
+        if time.perf_counter() - t0 >= budget_s:
+            break
+    dt = time.perf_counter() - t0
+    return flops_slice * n / dt / 1e12, n, dt, threads
+
+
+# ---------------------------------------------------------------------------
+# reference arm: the CPU path on the host cores of rank 0
+# ---------------------------------------------------------------------------
+def run_reference(args, wl: Workload):
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from oracle.attention_oracle import attention_fp32
+
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    B, N, H, d = wl.shape
+    g = torch.Generator().manual_seed(42)
+    q = (torch.randn(1, N, 1, d, generator=g) * wl.sigma_qk).to(wl.dtype)
+    k = (torch.randn(1, N, 1, d, generator=g) * wl.sigma_qk).to(wl.dtype)
+    v = torch.randn(1, N, 1, d, generator=g).to(wl.dtype)
+    for _ in range(args.warmup):
+        attention_fp32(q, k, v)
+    times = []
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        attention_fp32(q, k, v)
+        times.append(time.perf_counter() - t0)
+    per_slice = sum(times) / len(times)
+    slices = B * H
+    value = 4 * N * N * d / per_slice / 1e12
+    sample = f"one (batch, head) slice [{N}x{d}] per step of {slices} in the workload; TFLOP/s extrapolated linearly"
+    line = {
+        "impl": "reference",
+        "metric": METRIC,
+        "value": value,
+        "unit": "TFLOP/s",
+        "n_gpus": args.gpus,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": per_slice * slices * 1e3,
+        "higher_is_better": True,
+        "scaling": "strong",
+        "vs_baseline": None,
+        "dtype": wl.dtype_name(),
+        "data": "synthetic",
+        "config": workload_config(wl, args.gpus),
+        "cpu_baseline": {"value": value, "unit": "TFLOP/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(wl: Workload, n_gpus: int):
+    return {
+        "workload": wl.name,
+        "shape_BNHd": list(wl.shape),
+        "global_batch": wl.batch,
+        "seq_len": wl.seq_len,
+        "n_heads": wl.n_heads,
+        "head_dim": wl.d_head,
+        "causal": False,
+        "sigma_qk": wl.sigma_qk,
+        "parallelism": f"batch split over {n_gpus} GPU(s), no collective on the data path",
+        "l2": f"inputs {3 * wl.hbm_bytes // 4 / 1e9:.2f} GB > 126 MB L2, no flush between steps",
+    }
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def run_ours(args, wl: Workload):
+    import afa_flash_attention_kernels as fa
+    from afa_py.afa_config import AFAForwardKernelConfig, DType
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        log(f"warning: --gpus {args.gpus} but WORLD_SIZE={world}; using WORLD_SIZE")
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    if wl.batch % world != 0:
+        raise SystemExit(f"batch {wl.batch} is not divisible by {world} GPUs")
+    per = wl.batch // world
+    shard = slice(rank * per, (rank + 1) * per)
+
+    q, k, v = make_inputs(wl, seed=42, device=dev, batch_slice=shard)
+    o = torch.empty_like(q)
+    cfg = AFAForwardKernelConfig(dtype=DType.FP16 if wl.dtype == torch.float16 else DType.BF16, d_head=wl.d_head)
+    stream = torch.cuda.current_stream()
+    flops_rank = wl.flops // world
+    total_flops = flops_rank * world
+
+    def barrier():
+        torch.cuda.synchronize()
+        if dist is not None:
+            dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize()
+
+    def max_over_ranks(x: float) -> float:
+        if dist is None:
+            return x
+        t = torch.tensor([x], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    sampler = ClockSampler(local_rank) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+
+    # --- device-resident timing ------------------------------------------
+    for _ in range(args.warmup):
+        fa.forward(cfg, q, k, v, o, False)
+    barrier()
+    fa.check_status(local_rank)
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    barrier()
+    w0 = time.time()
+    for s, e in ev:
+        s.record(stream)
+        fa.forward(cfg, q, k, v, o, False)
+        e.record(stream)
+    barrier()
+    w1 = time.time()
+    fa.check_status(local_rank)
+    launch_ms = [s.elapsed_time(e) for s, e in ev]
+    ms_rank = sum(launch_ms) / len(launch_ms)
+    ms_step = max_over_ranks(ms_rank)
+    value = total_flops / (ms_step * 1e-3) / 1e12
+    kernel_tflops_rank = flops_rank / (ms_rank * 1e-3) / 1e12
+
+    # --- end to end through the public API ----------------------------------
+    qh, kh, vh = (t.cpu().pin_memory() for t in (q, k, v))
+    oh = torch.empty(q.shape, dtype=q.dtype).pin_memory()
+    e2e_steps = max(1, min(args.steps, args.e2e_steps))
+    for _ in range(min(2, args.warmup)):
+        qd, kd, vd = (t.to(dev, non_blocking=True) for t in (qh, kh, vh))
+        od, _ = fa.forward(cfg, qd, kd, vd, None, False)
+        oh.copy_(od, non_blocking=True)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier()
+    x0 = time.time()
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        qd, kd, vd = (t.to(dev, non_blocking=True) for t in (qh, kh, vh))
+        od, _ = fa.forward(cfg, qd, kd, vd, None, False)
+        oh.copy_(od, non_blocking=True)
+    e1.record(stream)
+    barrier()
+    x1 = time.time()
+    fa.check_status(local_rank)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps)
+    e2e_value = total_flops / (e2e_ms * 1e-3) / 1e12
+    h2d = 3 * q.numel() * q.element_size()
+    d2h = o.numel() * o.element_size()
+
+    clocks = None
+    if sampler:
+        sampler.stop()
+        clocks = sampler.summary([(w0, w1), (x0, x1)])
+
+    # --- CPU baseline (rank 0, N = 1 only) -------------------------------------
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rate, n, secs, threads = cpu_attention_rate(wl, args.cpu_budget)
+        cpu = {
+            "value": rate,
+            "unit": "TFLOP/s",
+            "cores": threads,
+            "kind": "port",
+            "sample": f"{n} (batch, head) slices [{wl.seq_len}x{wl.d_head}] of {wl.batch * wl.n_heads} in {secs:.1f} s, "
+                      "naive torch fp32 softmax(QK^T*scale)V, extrapolated linearly",
+        }
+
+    if rank == 0:
+        peaks, peak_src = load_peaks()
+        peak = float(peaks.get("bf16_tflops", FALLBACK_PEAK["bf16_tflops"]))
+        traffic = load_traffic(wl.name)
+        if traffic is not None and world > 1:
+            traffic = traffic // world
+        line = {
+            "metric": METRIC,
+            "value": value,
+            "unit": "TFLOP/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms_step,
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": None,
+            "dtype": wl.dtype_name(),
+            "data": "synthetic",
+            "config": workload_config(wl, world),
+            "frac_of_nominal_dense_peak": value / (NOMINAL_DENSE_TFLOPS * world),
+            "roofline": {
+                "bound": "tensor",
+                "achieved": kernel_tflops_rank,
+                "peak": peak,
+                "unit": "TFLOP/s",
+                "frac": kernel_tflops_rank / peak,
+                "peak_source": f"{peak_src} dense bf16 (burst, MEASURED_PEAKS.json)" if peak_src == "measured" else "fallback 1.59 PFLOP/s",
+                "traffic": traffic,
+                "algorithmic_bytes": wl.hbm_bytes // world,
+                "hbm_gbs": wl.hbm_bytes / world / (ms_rank * 1e-3) / 1e9,
+            },
+            "e2e": {"value": e2e_value, "unit": "TFLOP/s", "h2d_bytes_per_step": h2d * world, "d2h_bytes_per_step": d2h * world,
+                    "ms_per_step": e2e_ms, "steps": e2e_steps},
+            "gpu_launches": args.steps,
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+            "launch_ms": {"min": min(launch_ms), "median": statistics.median(launch_ms), "max": max(launch_ms)},
+        }
+        print(json.dumps(line), flush=True)
+
+    if dist is not None:
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__.splitlines()[0])
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--config", choices=sorted(WORKLOADS), default="cfg4")
+    ap.add_argument("--e2e-steps", type=int, default=10)
+    ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU-baseline work")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(3, args.warmup)  # at least 3 untimed warm-up steps (reported as used)
+    wl = WORKLOADS[args.config]
+    if args.impl == "reference":
+        run_reference(args, wl)
+    else:
+        run_ours(args, wl)
+
+
+if __name__ == "__main__":
+    main()
