@@ -102,8 +102,15 @@ struct FwdLayout {
   static constexpr int kBarKVFull = 2;                   // [kStages]
   static constexpr int kBarKVEmpty = 2 + kStages;        // [kStages]
   static constexpr int kBarSFull = 2 + 2 * kStages;      // [2]
-  static constexpr int kBarPReady = kBarSFull + 2;       // [2]
-  static constexpr int kBarOFinal = kBarPReady + 2;      // [2]
+  // P is handed to the PV MMA in kPChunks column chunks, one barrier each, so
+  // the tensor core starts O += P V on the first chunk while the softmax
+  // warpgroup is still computing the rest.
+  static constexpr int kPChunks = 4;
+  static constexpr int kSColsPerChunk = kBN / kPChunks;       // 32 S columns
+  static constexpr int kPColsPerChunk = kSColsPerChunk / 2;   // 16 TMEM columns of packed P
+  static constexpr int kPvStepsPerChunk = kSColsPerChunk / 16;  // 2 MMA K-steps
+  static constexpr int kBarPReady = kBarSFull + 2;       // [2][kPChunks]
+  static constexpr int kBarOFinal = kBarPReady + 2 * kPChunks;  // [2]
   static constexpr int kBarMmaDrain = kBarOFinal + 2;
   static constexpr int kNumBars = kBarMmaDrain + 1;
   static constexpr uint32_t kOffTmemSlot = kOffBar + kNumBars * 8;
@@ -147,19 +154,21 @@ struct CtaSync {
   }
 
   // honour_abort = false is used by teardown drains, which must run to the end.
+  // Waiting threads are suspended by the hardware between checks (up to
+  // kSuspendNs each), so idle warps do not take issue slots from the warps
+  // that share their SM sub-partition.
   __device__ __forceinline__ bool wait_slow(uint32_t bar, uint32_t parity, int site,
-                                         bool honour_abort) const {
+                                            bool honour_abort) const {
+    constexpr uint32_t kSuspendNs = 200000;  // 0.2 ms per suspended check
     const uint64_t t0 = globaltimer_ns();
     for (uint32_t it = 1;; ++it) {
-      if (mbar_try_wait(bar, parity)) return true;
-      if ((it & 127u) == 0u) {
-        if (honour_abort && *abort_flag) return false;
-        const uint64_t dt = globaltimer_ns() - t0;
-        if (dt > timeout_ns || it > (1u << 30)) {
-          *abort_flag = 1;
-          if (status != nullptr) atomicCAS(status, 0, AFA_DEV_TIMEOUT_BASE + site);
-          return false;
-        }
+      if (mbar_try_wait_suspend(bar, parity, kSuspendNs)) return true;
+      if (honour_abort && *abort_flag) return false;
+      const uint64_t dt = globaltimer_ns() - t0;
+      if (dt > timeout_ns || it > (1u << 30)) {
+        *abort_flag = 1;
+        if (status != nullptr) atomicCAS(status, 0, AFA_DEV_TIMEOUT_BASE + site);
+        return false;
       }
     }
   }
@@ -220,21 +229,24 @@ __device__ __forceinline__ void role_load(const FwdParams& p, uint32_t sbase, ui
   auto bar = [&](int i) { return bar0 + 8u * static_cast<uint32_t>(i); };
   const uint64_t pol_kv = l2_policy_evict_last();
   const uint64_t pol_q = l2_policy_evict_first();
+  // The whole warp runs this role in converged control flow; lane 0 issues.
+  const bool leader = (threadIdx.x & 31u) == 0u;
   uint32_t kv_cnt = 0;
   uint32_t it = 0;
   for (int w = blockIdx.x; w < p.n_work; w += gridDim.x, ++it) {
     int qp, h, b;
     decode_work(w, p.n_q_pairs, p.n_heads, qp, h, b);
     if (!sy.wait(bar(L::kBarQEmpty), (it & 1u) ^ 1u, kSiteLoadQEmpty)) return;
-    mbar_arrive_expect_tx(bar(L::kBarQFull), 2u * L::kTileBytes);
+    if (leader) mbar_arrive_expect_tx(bar(L::kBarQFull), 2u * L::kTileBytes);
 #pragma unroll
     for (int t = 0; t < 2; ++t) {
 #pragma unroll
       for (int a = 0; a < L::kAtoms; ++a) {
         const int row0 = qp * 256 + t * 128;
         const bool si = (p.seq_inner_mask & 1u) != 0u;
-        tma_load_4d(sbase + L::kOffQ + t * L::kTileBytes + a * L::kAtomBytes, &p.tm_q,
-                    bar(L::kBarQFull), a * 64, si ? row0 : h, si ? h : row0, b, pol_q);
+        if (leader)
+          tma_load_4d(sbase + L::kOffQ + t * L::kTileBytes + a * L::kAtomBytes, &p.tm_q,
+                      bar(L::kBarQFull), a * 64, si ? row0 : h, si ? h : row0, b, pol_q);
       }
     }
     for (int j = 0; j < p.n_kv; ++j) {
@@ -243,14 +255,15 @@ __device__ __forceinline__ void role_load(const FwdParams& p, uint32_t sbase, ui
         const uint32_t slot = kv_cnt % kStages;
         const uint32_t ph = (kv_cnt / kStages) & 1u;
         if (!sy.wait(bar(L::kBarKVEmpty + slot), ph ^ 1u, kSiteLoadKVEmpty)) return;
-        mbar_arrive_expect_tx(bar(L::kBarKVFull + slot), L::kTileBytes);
+        if (leader) mbar_arrive_expect_tx(bar(L::kBarKVFull + slot), L::kTileBytes);
         const CUtensorMap* map = kv ? &p.tm_v : &p.tm_k;
         const bool si = (p.seq_inner_mask & (kv ? 4u : 2u)) != 0u;
         const int row0 = j * 128;
 #pragma unroll
         for (int a = 0; a < L::kAtoms; ++a) {
-          tma_load_4d(sbase + L::kOffKV + slot * L::kTileBytes + a * L::kAtomBytes, map,
-                      bar(L::kBarKVFull + slot), a * 64, si ? row0 : h, si ? h : row0, b, pol_kv);
+          if (leader)
+            tma_load_4d(sbase + L::kOffKV + slot * L::kTileBytes + a * L::kAtomBytes, map,
+                        bar(L::kBarKVFull + slot), a * 64, si ? row0 : h, si ? h : row0, b, pol_kv);
         }
         ++kv_cnt;
       }
@@ -262,7 +275,8 @@ __device__ __forceinline__ void role_load(const FwdParams& p, uint32_t sbase, ui
 // Role: MMA issuer (one thread)
 // ---------------------------------------------------------------------------
 template <int kD, bool kBF16, int kStages>
-__device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t q_addr, uint32_t k_addr) {
+__device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t q_addr, uint32_t k_addr,
+                                         uint32_t issue) {
   using L = FwdLayout<kD, kBF16, kStages>;
   constexpr uint32_t kIdesc = idesc_f16_f32(128, 128, kBF16, false);
 #pragma unroll
@@ -271,22 +285,24 @@ __device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t q_addr, uint3
     // then the next atom (next TMA box) for head_dim >= 64.
     const uint32_t off = (k / 4) * L::kAtomBytes + (k % 4) * 32u;
     umma_f16_ss(d_tmem, sdesc_lo(q_addr + off, 16), sdesc_lo(k_addr + off, 16), kIdesc,
-                k > 0 ? 1u : 0u);
+                k > 0 ? 1u : 0u, issue);
   }
 }
 
+// O (+)= P[:, chunk] V[chunk, :] for one P chunk (kPvStepsPerChunk K-steps).
 template <int kD, bool kBF16, int kStages>
-__device__ __forceinline__ void issue_pv(uint32_t d_tmem, uint32_t p_tmem, uint32_t v_addr,
-                                         bool accumulate) {
+__device__ __forceinline__ void issue_pv_chunk(uint32_t d_tmem, uint32_t p_tmem, uint32_t v_addr,
+                                               int chunk, bool accumulate, uint32_t issue) {
   using L = FwdLayout<kD, kBF16, kStages>;
   constexpr uint32_t kIdesc = idesc_f16_f32(128, kD, kBF16, true);
 #pragma unroll
-  for (int k = 0; k < L::kBN / 16; ++k) {
+  for (int i = 0; i < L::kPvStepsPerChunk; ++i) {
+    const int k = chunk * L::kPvStepsPerChunk + i;
     // V is MN-major (head_dim contiguous): 8-row groups 1024 B apart (SBO),
     // 64-element head_dim atoms one TMA box apart (LBO); 16 key rows per step.
     // P in TMEM: 16 elements of 16 bit = 8 columns per K step.
     umma_f16_ts(d_tmem, p_tmem + k * 8u, sdesc_lo(v_addr + k * 16u * 128u, L::kAtomBytes), kIdesc,
-                (accumulate || k > 0) ? 1u : 0u);
+                (accumulate || i > 0) ? 1u : 0u, issue);
   }
 }
 
@@ -296,21 +312,36 @@ __device__ __forceinline__ void role_mma(const FwdParams& p, uint32_t sbase, uin
   using L = FwdLayout<kD, kBF16, kStages>;
   auto bar = [&](int i) { return bar0 + 8u * static_cast<uint32_t>(i); };
   auto slot_addr = [&](uint32_t s) { return sbase + L::kOffKV + s * L::kTileBytes; };
-  const uint32_t tS0 = tmem + 0u, tS1 = tmem + 128u;
-  const uint32_t tO0 = tmem + L::kColO, tO1 = tmem + L::kColO + kD;
-  const uint32_t q0 = sbase + L::kOffQ, q1 = q0 + L::kTileBytes;
-  uint32_t kv_cnt = 0, it = 0, pph0 = 0, pph1 = 0;
+  const uint32_t tS[2] = {tmem + 0u, tmem + 128u};
+  const uint32_t tO[2] = {tmem + L::kColO, tmem + L::kColO + kD};
+  const uint32_t qa[2] = {sbase + L::kOffQ, sbase + L::kOffQ + L::kTileBytes};
+  // The whole warp runs this role in converged control flow; lane 0 issues.
+  const uint32_t leader = (threadIdx.x & 31u) == 0u ? 1u : 0u;
+  uint32_t kv_cnt = 0, it = 0;
+  uint32_t pph[2] = {0u, 0u};
+  // O_wg (+)= P_wg V: each P chunk is issued as soon as its barrier flips.
+  auto pv = [&](int wg, uint32_t v_addr, bool accumulate) -> bool {
+#pragma unroll
+    for (int c = 0; c < L::kPChunks; ++c) {
+      if (!sy.wait(bar(L::kBarPReady + wg * L::kPChunks + c), pph[wg], wg ? kSiteMmaP1 : kSiteMmaP0))
+        return false;
+      tc_fence_after_sync();
+      issue_pv_chunk<kD, kBF16, kStages>(tO[wg], tS[wg], v_addr, c, accumulate || c > 0, leader);
+    }
+    pph[wg] ^= 1u;
+    return true;
+  };
   bool ok = true;
   for (int w = blockIdx.x; w < p.n_work && ok; w += gridDim.x, ++it) {
     if (!sy.wait(bar(L::kBarQFull), it & 1u, kSiteMmaQFull)) { ok = false; break; }
     uint32_t ks = kv_cnt % kStages;
     if (!sy.wait(bar(L::kBarKVFull + ks), (kv_cnt / kStages) & 1u, kSiteMmaKFull)) { ok = false; break; }
     tc_fence_after_sync();
-    issue_qk<kD, kBF16, kStages>(tS0, q0, slot_addr(ks));
-    umma_commit(bar(L::kBarSFull + 0));
-    issue_qk<kD, kBF16, kStages>(tS1, q1, slot_addr(ks));
-    umma_commit(bar(L::kBarSFull + 1));
-    umma_commit(bar(L::kBarKVEmpty + ks));
+    issue_qk<kD, kBF16, kStages>(tS[0], qa[0], slot_addr(ks), leader);
+    umma_commit(bar(L::kBarSFull + 0), leader);
+    issue_qk<kD, kBF16, kStages>(tS[1], qa[1], slot_addr(ks), leader);
+    umma_commit(bar(L::kBarSFull + 1), leader);
+    umma_commit(bar(L::kBarKVEmpty + ks), leader);
     ++kv_cnt;
     uint32_t vcnt = kv_cnt++;
     for (int j = 1; j < p.n_kv; ++j) {
@@ -318,42 +349,32 @@ __device__ __forceinline__ void role_mma(const FwdParams& p, uint32_t sbase, uin
       const uint32_t vs = vcnt % kStages;
       if (!sy.wait(bar(L::kBarKVFull + vs), (vcnt / kStages) & 1u, kSiteMmaVFull)) { ok = false; break; }
       if (!sy.wait(bar(L::kBarKVFull + ks), (kv_cnt / kStages) & 1u, kSiteMmaKFull)) { ok = false; break; }
-      if (!sy.wait(bar(L::kBarPReady + 0), pph0, kSiteMmaP0)) { ok = false; break; }
-      pph0 ^= 1u;
-      tc_fence_after_sync();
-      issue_pv<kD, kBF16, kStages>(tO0, tS0, slot_addr(vs), j > 1);
-      issue_qk<kD, kBF16, kStages>(tS0, q0, slot_addr(ks));
-      umma_commit(bar(L::kBarSFull + 0));
-      if (!sy.wait(bar(L::kBarPReady + 1), pph1, kSiteMmaP1)) { ok = false; break; }
-      pph1 ^= 1u;
-      tc_fence_after_sync();
-      issue_pv<kD, kBF16, kStages>(tO1, tS1, slot_addr(vs), j > 1);
-      umma_commit(bar(L::kBarKVEmpty + vs));
-      issue_qk<kD, kBF16, kStages>(tS1, q1, slot_addr(ks));
-      umma_commit(bar(L::kBarSFull + 1));
-      umma_commit(bar(L::kBarKVEmpty + ks));
+      // Tensor-core order PV0(j-1), S0(j), PV1(j-1), S1(j): S_i(j) overwrites
+      // the TMEM columns P_i(j-1) was read from, after that PV in issue order.
+      if (!pv(0, slot_addr(vs), j > 1)) { ok = false; break; }
+      issue_qk<kD, kBF16, kStages>(tS[0], qa[0], slot_addr(ks), leader);
+      umma_commit(bar(L::kBarSFull + 0), leader);
+      if (!pv(1, slot_addr(vs), j > 1)) { ok = false; break; }
+      umma_commit(bar(L::kBarKVEmpty + vs), leader);
+      issue_qk<kD, kBF16, kStages>(tS[1], qa[1], slot_addr(ks), leader);
+      umma_commit(bar(L::kBarSFull + 1), leader);
+      umma_commit(bar(L::kBarKVEmpty + ks), leader);
       ++kv_cnt;
       vcnt = kv_cnt++;
     }
     if (!ok) break;
-    umma_commit(bar(L::kBarQEmpty));  // all S MMAs of this work item issued: Q may be reloaded
+    umma_commit(bar(L::kBarQEmpty), leader);  // all S MMAs of this work item issued: Q may be reloaded
     const uint32_t vs = vcnt % kStages;
     if (!sy.wait(bar(L::kBarKVFull + vs), (vcnt / kStages) & 1u, kSiteMmaVFull)) { ok = false; break; }
-    if (!sy.wait(bar(L::kBarPReady + 0), pph0, kSiteMmaP0)) { ok = false; break; }
-    pph0 ^= 1u;
-    tc_fence_after_sync();
-    issue_pv<kD, kBF16, kStages>(tO0, tS0, slot_addr(vs), p.n_kv > 1);
-    umma_commit(bar(L::kBarOFinal + 0));
-    if (!sy.wait(bar(L::kBarPReady + 1), pph1, kSiteMmaP1)) { ok = false; break; }
-    pph1 ^= 1u;
-    tc_fence_after_sync();
-    issue_pv<kD, kBF16, kStages>(tO1, tS1, slot_addr(vs), p.n_kv > 1);
-    umma_commit(bar(L::kBarOFinal + 1));
-    umma_commit(bar(L::kBarKVEmpty + vs));
+    if (!pv(0, slot_addr(vs), p.n_kv > 1)) { ok = false; break; }
+    umma_commit(bar(L::kBarOFinal + 0), leader);
+    if (!pv(1, slot_addr(vs), p.n_kv > 1)) { ok = false; break; }
+    umma_commit(bar(L::kBarOFinal + 1), leader);
+    umma_commit(bar(L::kBarKVEmpty + vs), leader);
   }
   // Drain: every MMA issued by this thread has completed before teardown
   // releases tensor memory.
-  umma_commit(bar(L::kBarMmaDrain));
+  umma_commit(bar(L::kBarMmaDrain), leader);
   if (!mbar_try_wait(bar(L::kBarMmaDrain), 0)) sy.wait_slow(bar(L::kBarMmaDrain), 0, kSiteMmaDrain, false);
 }
 
@@ -373,7 +394,8 @@ __device__ __forceinline__ void role_softmax(const FwdParams& p, int wg, uint32_
   const uint32_t tO = tmem + lane_field + L::kColO + static_cast<uint32_t>(wg) * kD;
   const float sl2 = p.scale_log2;
   const uint32_t bar_s = bar(L::kBarSFull + wg);
-  const uint32_t bar_p = bar(L::kBarPReady + wg);
+  const uint32_t bar_p0 = bar(L::kBarPReady + wg * L::kPChunks);
+  const uint32_t lane = threadIdx.x & 31u;
   const uint32_t bar_o = bar(L::kBarOFinal + wg);
   uint32_t sph = 0, oph = 0;
 
@@ -410,35 +432,10 @@ __device__ __forceinline__ void role_softmax(const FwdParams& p, int wg, uint32_
       const bool need = m_new > m_ref + 8.0f;
       // alpha rescales the running sum and O from the old reference max.
       const float alpha = need ? ex2_approx(m_ref - m_new) : 1.0f;
-      if (need) m_ref = m_new;
-      uint32_t pk[64];
-      const float2 c2 = make_float2(sl2, sl2);
-      const float2 nm2 = make_float2(-m_ref, -m_ref);
-      float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
-#pragma unroll
-      for (int k = 0; k < 128; k += 2) {
-        const float2 x = __ffma2_rn(make_float2(s[k], s[k + 1]), c2, nm2);
-        float2 e;
-        if (((k >> 1) & 7) < L::kEmuPairs) {
-          e = exp2_fma_pipe2(x);
-        } else {
-          e.x = ex2_approx(x.x);
-          e.y = ex2_approx(x.y);
-        }
-        if ((k >> 1) & 1)
-          acc1 = __fadd2_rn(acc1, e);
-        else
-          acc0 = __fadd2_rn(acc0, e);
-        pk[k >> 1] = pack2<kBF16>(e.x, e.y);
-      }
-      const float ls0 = acc0.x + acc1.x, ls1 = acc0.y + acc1.y;
-      l = l * alpha + (ls0 + ls1);
-      tmem_st32(tS, *reinterpret_cast<uint32_t(*)[32]>(&pk[0]));
-      tmem_st32(tS + 32u, *reinterpret_cast<uint32_t(*)[32]>(&pk[32]));
       if (j > 0 && __any_sync(0xffffffffu, need)) {
-        // Conditional rescale of O.  The previous PV of this tile has
-        // completed (it was committed before S(j)), and the next one waits for
-        // this warpgroup's p_ready: O is quiescent here.
+        // Conditional rescale of O, before this step's first P chunk is handed
+        // over: the previous PV of this tile has completed (it was committed
+        // before S(j)) and the next one waits for that chunk, so O is quiescent.
 #pragma unroll
         for (int c = 0; c < kD / 32; ++c) {
           uint32_t o[32];
@@ -448,9 +445,49 @@ __device__ __forceinline__ void role_softmax(const FwdParams& p, int wg, uint32_
           tmem_st32(tO + c * 32u, o);
         }
       }
-      tmem_wait_st();
-      tc_fence_before_sync();
-      mbar_arrive(bar_p);
+      if (need) m_ref = m_new;
+      const float2 c2 = make_float2(sl2, sl2);
+      const float2 nm2 = make_float2(-m_ref, -m_ref);
+      float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
+      uint32_t pk[64];
+      // P = exp2(S * scale*log2e - m_ref) for one chunk of kSColsPerChunk columns.
+      auto exp_chunk = [&](int c) {
+#pragma unroll
+        for (int k = c * L::kSColsPerChunk; k < (c + 1) * L::kSColsPerChunk; k += 2) {
+          const float2 x = __ffma2_rn(make_float2(s[k], s[k + 1]), c2, nm2);
+          float2 e;
+          if (((k >> 1) & 7) < L::kEmuPairs) {
+            e = exp2_fma_pipe2(x);
+          } else {
+            e.x = ex2_approx(x.x);
+            e.y = ex2_approx(x.y);
+          }
+          if ((k >> 1) & 1)
+            acc1 = __fadd2_rn(acc1, e);
+          else
+            acc0 = __fadd2_rn(acc0, e);
+          pk[k >> 1] = pack2<kBF16>(e.x, e.y);
+        }
+      };
+      // Chunk c's P is in TMEM (and any O rescale done): release it to the MMA.
+      auto hand_off = [&](int c) {
+        tmem_wait_st();
+        tc_fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_p0 + 8u * static_cast<uint32_t>(c));
+      };
+      // Software-pipelined by one chunk: the store of chunk c-1 drains while
+      // chunk c is computed.
+      exp_chunk(0);
+      tmem_st16(tS, &pk[0]);
+#pragma unroll
+      for (int c = 1; c < L::kPChunks; ++c) {
+        exp_chunk(c);
+        hand_off(c - 1);
+        tmem_st16(tS + c * L::kPColsPerChunk, &pk[c * L::kPColsPerChunk]);
+      }
+      hand_off(L::kPChunks - 1);
+      l = l * alpha + ((acc0.x + acc1.x) + (acc0.y + acc1.y));
     }
     // Epilogue: O / l, round to the input type, store the row.
     if (!sy.wait(bar_o, oph, kSiteSoftmaxO)) return;
@@ -498,7 +535,8 @@ __global__ void __launch_bounds__(384, 1) afa_fwd_sm100_kernel(const __grid_cons
 
   if (warp == 0 && lane == 0) {
     for (int i = 0; i < L::kNumBars; ++i) {
-      const uint32_t count = (i == L::kBarPReady || i == L::kBarPReady + 1) ? L::kSoftmaxThreads : 1u;
+      // p_ready: one elected arrival per softmax warp; all others: one arrival.
+      const uint32_t count = (i >= L::kBarPReady && i < L::kBarPReady + 2 * L::kPChunks) ? 4u : 1u;
       mbar_init(bar0 + 8u * i, count);
     }
     *abort_flag = 0;
@@ -520,9 +558,9 @@ __global__ void __launch_bounds__(384, 1) afa_fwd_sm100_kernel(const __grid_cons
   if (warp < 4) {
     setmaxnreg_dec<L::kProducerRegs>();
     if (warp == 0) {
-      if (lane == 0) role_load<kD, kBF16, kStages>(p, sbase, bar0, sy);
+      role_load<kD, kBF16, kStages>(p, sbase, bar0, sy);
     } else if (warp == 1) {
-      if (lane == 0) role_mma<kD, kBF16, kStages>(p, sbase, bar0, tmem, sy);
+      role_mma<kD, kBF16, kStages>(p, sbase, bar0, tmem, sy);
     }
   } else {
     setmaxnreg_inc<L::kSoftmaxRegs>();

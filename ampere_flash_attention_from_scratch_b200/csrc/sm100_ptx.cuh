@@ -79,6 +79,22 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
+// As mbar_try_wait, but the thread may be suspended (not spinning) for up to
+// `suspend_ns` while the phase is incomplete; the hardware resumes it when the
+// phase completes.
+__device__ __forceinline__ bool mbar_try_wait_suspend(uint32_t bar, uint32_t parity,
+                                                      uint32_t suspend_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}\n"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity), "r"(suspend_ns)
+      : "memory");
+  return ok != 0;
+}
+
 // ---------------------------------------------------------------------------
 // TMA (bulk tensor copies).  Never used with .multicast::cluster.
 // ---------------------------------------------------------------------------
@@ -173,37 +189,45 @@ __host__ __device__ constexpr uint32_t idesc_f16_f32(int M, int N, bool bf16, bo
          (static_cast<uint32_t>(M >> 4) << 24);
 }
 
+// The MMA-issue helpers below are called by a whole warp in converged
+// control flow, so every operand is warp-uniform (uniform registers); only
+// the lane whose `issue` is non-zero executes the instruction.
+
 // D[tmem] (+)= A[smem] * B[smem]; operands given by descriptor low words.
 __device__ __forceinline__ void umma_f16_ss(uint32_t d_tmem, uint32_t a_lo, uint32_t b_lo,
-                                            uint32_t idesc, uint32_t accumulate) {
+                                            uint32_t idesc, uint32_t accumulate, uint32_t issue) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\t.reg .b64 da, db;\n\t"
+      "{\n\t.reg .pred p, q;\n\t.reg .b64 da, db;\n\t"
       "mov.b64 da, {%1, %5};\n\t"
       "mov.b64 db, {%2, %5};\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %3, p;\n\t}\n" ::"r"(d_tmem),
-      "r"(a_lo), "r"(b_lo), "r"(idesc), "r"(accumulate), "n"(kDescHiSw128)
+      "setp.ne.b32 q, %6, 0;\n\t"
+      "@q tcgen05.mma.cta_group::1.kind::f16 [%0], da, db, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_lo), "r"(b_lo), "r"(idesc), "r"(accumulate), "n"(kDescHiSw128), "r"(issue)
       : "memory");
 }
 
 // D[tmem] (+)= A[tmem] * B[smem]
 __device__ __forceinline__ void umma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint32_t b_lo,
-                                            uint32_t idesc, uint32_t accumulate) {
+                                            uint32_t idesc, uint32_t accumulate, uint32_t issue) {
   asm volatile(
-      "{\n\t.reg .pred p;\n\t.reg .b64 db;\n\t"
+      "{\n\t.reg .pred p, q;\n\t.reg .b64 db;\n\t"
       "mov.b64 db, {%2, %5};\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], db, %3, p;\n\t}\n" ::"r"(d_tmem),
-      "r"(a_tmem), "r"(b_lo), "r"(idesc), "r"(accumulate), "n"(kDescHiSw128)
+      "setp.ne.b32 q, %6, 0;\n\t"
+      "@q tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], db, %3, p;\n\t}\n" ::"r"(d_tmem),
+      "r"(a_tmem), "r"(b_lo), "r"(idesc), "r"(accumulate), "n"(kDescHiSw128), "r"(issue)
       : "memory");
 }
 
 // Arrive (once) on `bar` when all previously issued tcgen05 async ops of this
 // thread have completed.
-__device__ __forceinline__ void umma_commit(uint32_t bar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
-                   bar)
-               : "memory");
+__device__ __forceinline__ void umma_commit(uint32_t bar, uint32_t issue) {
+  asm volatile(
+      "{\n\t.reg .pred q;\n\tsetp.ne.b32 q, %1, 0;\n\t"
+      "@q tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n\t}\n" ::"r"(bar),
+      "r"(issue)
+      : "memory");
 }
 
 // ---------------------------------------------------------------------------
