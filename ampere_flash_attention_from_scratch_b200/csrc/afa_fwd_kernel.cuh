@@ -105,10 +105,13 @@ struct FwdLayout {
   // P is handed to the PV MMA in kPChunks column chunks, one barrier each, so
   // the tensor core starts O += P V on the first chunk while the softmax
   // warpgroup is still computing the rest.
-  static constexpr int kPChunks = 4;
-  static constexpr int kSColsPerChunk = kBN / kPChunks;       // 32 S columns
-  static constexpr int kPColsPerChunk = kSColsPerChunk / 2;   // 16 TMEM columns of packed P
-  static constexpr int kPvStepsPerChunk = kSColsPerChunk / 16;  // 2 MMA K-steps
+#ifndef AFA_P_CHUNKS
+#define AFA_P_CHUNKS 2
+#endif
+  static constexpr int kPChunks = AFA_P_CHUNKS;
+  static constexpr int kSColsPerChunk = kBN / kPChunks;       // S columns per chunk
+  static constexpr int kPColsPerChunk = kSColsPerChunk / 2;   // TMEM columns of packed P
+  static constexpr int kPvStepsPerChunk = kSColsPerChunk / 16;  // MMA K-steps per chunk
   static constexpr int kBarPReady = kBarSFull + 2;       // [2][kPChunks]
   static constexpr int kBarOFinal = kBarPReady + 2 * kPChunks;  // [2]
   static constexpr int kBarMmaDrain = kBarOFinal + 2;
@@ -129,8 +132,8 @@ struct FwdLayout {
   static constexpr int kSoftmaxRegs = 216;
   static_assert(kProducerRegs + 2 * kSoftmaxRegs <= 3 * kLaunchRegs, "register split too large");
   // Share of exp2 evaluations moved from the MUFU unit to the FMA pipe: in
-  // every group of 8 consecutive column pairs, the first kEmuPairs use the
-  // polynomial.  At head_dim 128 the MUFU work per K/V tile equals the MMA
+  // every group of 8 consecutive column pairs, kEmuPairs evenly spaced pairs
+  // use the polynomial (0 by default: every share measured so far was slower).  At head_dim 128 the MUFU work per K/V tile equals the MMA
   // work; at 64 it is twice the MMA work.
 #ifndef AFA_EXP_EMU_PAIRS_D128
 #define AFA_EXP_EMU_PAIRS_D128 0
@@ -456,7 +459,7 @@ __device__ __forceinline__ void role_softmax(const FwdParams& p, int wg, uint32_
         for (int k = c * L::kSColsPerChunk; k < (c + 1) * L::kSColsPerChunk; k += 2) {
           const float2 x = __ffma2_rn(make_float2(s[k], s[k + 1]), c2, nm2);
           float2 e;
-          if (((k >> 1) & 7) < L::kEmuPairs) {
+          if ((((k >> 1) * L::kEmuPairs) & 7) < L::kEmuPairs) {
             e = exp2_fma_pipe2(x);
           } else {
             e.x = ex2_approx(x.x);
@@ -478,13 +481,18 @@ __device__ __forceinline__ void role_softmax(const FwdParams& p, int wg, uint32_
       };
       // Software-pipelined by one chunk: the store of chunk c-1 drains while
       // chunk c is computed.
+      auto store_chunk = [&](int c) {
+#pragma unroll
+        for (int q = 0; q < L::kPColsPerChunk; q += 16)
+          tmem_st16(tS + c * L::kPColsPerChunk + q, &pk[c * L::kPColsPerChunk + q]);
+      };
       exp_chunk(0);
-      tmem_st16(tS, &pk[0]);
+      store_chunk(0);
 #pragma unroll
       for (int c = 1; c < L::kPChunks; ++c) {
         exp_chunk(c);
         hand_off(c - 1);
-        tmem_st16(tS + c * L::kPColsPerChunk, &pk[c * L::kPColsPerChunk]);
+        store_chunk(c);
       }
       hand_off(L::kPChunks - 1);
       l = l * alpha + ((acc0.x + acc1.x) + (acc0.y + acc1.y));
