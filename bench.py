@@ -40,7 +40,6 @@ import subprocess
 import sys
 import threading
 import time
-from datetime import timedelta
 from pathlib import Path
 
 import torch
@@ -248,22 +247,19 @@ def run_ours(args, wl: Workload):
     import afa_flash_attention_kernels as fa
     from afa_py.afa_config import AFAForwardKernelConfig, DType
 
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    rank = int(os.environ.get("RANK", "0"))
-    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    from ampere_flash_attention_from_scratch_b200 import multi_gpu
+
+    info = multi_gpu.rank_info_from_env()
+    world, rank, local_rank = info.world, info.rank, info.local_rank
     if world != args.gpus:
         log(f"warning: --gpus {args.gpus} but WORLD_SIZE={world}; using WORLD_SIZE")
     torch.cuda.set_device(local_rank)
     dev = torch.device("cuda", local_rank)
-    dist = None
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
-    if wl.batch % world != 0:
-        raise SystemExit(f"batch {wl.batch} is not divisible by {world} GPUs")
-    per = wl.batch // world
-    shard = slice(rank * per, (rank + 1) * per)
+    multi_gpu.init_process_group("nccl", info, timeout_s=300.0, device=dev)
+    try:
+        shard = multi_gpu.shard_range(wl.batch, world, rank)
+    except ValueError as e:
+        raise SystemExit(str(e))
 
     q, k, v = make_inputs(wl, seed=42, device=dev, batch_slice=shard)
     o = torch.empty_like(q)
@@ -274,16 +270,11 @@ def run_ours(args, wl: Workload):
 
     def barrier():
         torch.cuda.synchronize()
-        if dist is not None:
-            dist.barrier(device_ids=[local_rank])
+        multi_gpu.barrier(dev)
         torch.cuda.synchronize()
 
     def max_over_ranks(x: float) -> float:
-        if dist is None:
-            return x
-        t = torch.tensor([x], dtype=torch.float64, device=dev)
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+        return multi_gpu.max_over_ranks(x, dev)
 
     sampler = ClockSampler(local_rank) if rank == 0 else None
     if sampler:
@@ -396,9 +387,8 @@ def run_ours(args, wl: Workload):
         }
         print(json.dumps(line), flush=True)
 
-    if dist is not None:
-        dist.barrier(device_ids=[local_rank])
-        dist.destroy_process_group()
+    multi_gpu.barrier(dev)
+    multi_gpu.destroy()
 
 
 def main():
