@@ -5,7 +5,8 @@ At these sizes the CPU oracle would take hours, so parity is checked through
 (the same oracle code, run on device tensors), and (2) properties that hold at
 any size:
 * V = 1 everywhere  =>  O = 1 (softmax rows sum to one);
-* permuting the keys and values together leaves O unchanged.
+* permuting the keys and values together leaves O unchanged (two rounded
+  kernel outputs: each element within the absolute tolerance or one ulp).
 Tolerances as in test_forward_gpu.py (fp16 1e-2 / 1e-3, bf16 2e-2 / 2e-3).
 """
 
@@ -31,6 +32,19 @@ def _stats(a, b):
         tot += d.sum().item()
         n += d.numel()
     return mx, tot / n
+
+
+def _within_one_ulp_or_tol(a, b, dtype, tol):
+    """Every element of two rounded kernel outputs agrees within `tol` absolute
+    or one ulp of the output type at that element's magnitude (both outputs
+    carry their own final rounding)."""
+    rel = 2.0 ** -7 if dtype == torch.bfloat16 else 2.0 ** -10
+    for x, y in zip(a.reshape(a.shape[0], -1), b.reshape(b.shape[0], -1)):
+        d = (x.float() - y.float()).abs()
+        bound = torch.clamp(torch.maximum(x.float().abs(), y.float().abs()) * rel, min=tol)
+        if not bool((d <= bound).all()):
+            return False
+    return True
 
 
 def _cfg(wl):
@@ -85,6 +99,7 @@ def test_key_permutation_invariance(name):
     out_p = _run(wl, q, k[:, perm].contiguous(), v[:, perm].contiguous())
     mx, mean = _stats(out_p, out)
     tmax, tmean = TOL[wl.dtype]
-    assert mx <= tmax and mean <= tmean, f"{name}: max {mx:.3e} mean {mean:.3e}"
+    assert mean <= tmean, f"{name}: mean {mean:.3e}"
+    assert _within_one_ulp_or_tol(out_p, out, wl.dtype, tmax), f"{name}: max {mx:.3e}"
     del q, k, v, out, out_p
     torch.cuda.empty_cache()
