@@ -6,7 +6,7 @@ At these sizes the CPU oracle would take hours, so parity is checked through
 any size:
 * V = 1 everywhere  =>  O = 1 (softmax rows sum to one);
 * permuting the keys and values together leaves O unchanged (two rounded
-  kernel outputs: each element within the absolute tolerance or one ulp).
+  kernel outputs: each element within the absolute tolerance or 3 ulps).
 Tolerances as in test_forward_gpu.py (fp16 1e-2 / 1e-3, bf16 2e-2 / 2e-3).
 """
 
@@ -34,11 +34,13 @@ def _stats(a, b):
     return mx, tot / n
 
 
-def _within_one_ulp_or_tol(a, b, dtype, tol):
-    """Every element of two rounded kernel outputs agrees within `tol` absolute
-    or one ulp of the output type at that element's magnitude (both outputs
-    carry their own final rounding)."""
-    rel = 2.0 ** -7 if dtype == torch.bfloat16 else 2.0 ** -10
+def _within_ulps_or_tol(a, b, dtype, tol):
+    """Every element of two kernel outputs agrees within `tol` absolute or three
+    ulps of the output type at that element's magnitude: each output is within
+    about 1.5 ulp of the exact value (0.5 from its final rounding, about 1 from
+    rounding P to the input type, relative to a running maximum that evolves
+    differently when the keys are permuted)."""
+    rel = 3.0 * (2.0 ** -7 if dtype == torch.bfloat16 else 2.0 ** -10)
     for x, y in zip(a.reshape(a.shape[0], -1), b.reshape(b.shape[0], -1)):
         d = (x.float() - y.float()).abs()
         bound = torch.clamp(torch.maximum(x.float().abs(), y.float().abs()) * rel, min=tol)
@@ -100,6 +102,6 @@ def test_key_permutation_invariance(name):
     mx, mean = _stats(out_p, out)
     tmax, tmean = TOL[wl.dtype]
     assert mean <= tmean, f"{name}: mean {mean:.3e}"
-    assert _within_one_ulp_or_tol(out_p, out, wl.dtype, tmax), f"{name}: max {mx:.3e}"
+    assert _within_ulps_or_tol(out_p, out, wl.dtype, tmax), f"{name}: max {mx:.3e}"
     del q, k, v, out, out_p
     torch.cuda.empty_cache()
