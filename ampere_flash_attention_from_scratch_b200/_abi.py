@@ -27,6 +27,7 @@ AFA_ERR_LAUNCH = 8
 AFA_ERR_DEVICE_TIMEOUT = 9
 AFA_ERR_TOO_LARGE = 10
 AFA_DEV_TIMEOUT_BASE = 0x100
+AFA_TEST_PRODUCER_IDLE = 1
 
 # Every extern "C" symbol declared in include/afa_sm100.h.
 EXPORTED_SYMBOLS = (
@@ -58,6 +59,7 @@ class AfaFwdArgs(ctypes.Structure):
         ("scale", ctypes.c_float),
         ("status", ctypes.c_void_p),
         ("timeout_ns", ctypes.c_uint64),
+        ("test_flags", ctypes.c_uint32),
     ]
 
 
@@ -89,7 +91,7 @@ def load() -> ctypes.CDLL:
     return _lib
 
 
-def make_args(q, k, v, o, status=None, scale=0.0, timeout_ns=0) -> AfaFwdArgs:
+def make_args(q, k, v, o, status=None, scale=0.0, timeout_ns=0, test_flags=0) -> AfaFwdArgs:
     """AfaFwdArgs for torch tensors q, k, v, o of shape [B, N, H, d] (device memory)."""
     dt = {"torch.float16": AFA_DTYPE_FP16, "torch.bfloat16": AFA_DTYPE_BF16}.get(str(q.dtype), -1)
     a = AfaFwdArgs()
@@ -101,6 +103,7 @@ def make_args(q, k, v, o, status=None, scale=0.0, timeout_ns=0) -> AfaFwdArgs:
     a.scale = float(scale)
     a.status = status.data_ptr() if status is not None else None
     a.timeout_ns = int(timeout_ns)
+    a.test_flags = int(test_flags)
     return a
 
 

@@ -68,6 +68,7 @@ struct FwdParams {
   float scale_log2;  // scale * log2(e)
   int* status;
   unsigned long long timeout_ns;
+  unsigned test_flags;  // bit 0: the producer issues no loads (exercises the timeout path)
 };
 
 // Bounded-wait sites, reported as AFA_DEV_TIMEOUT_BASE + site.
@@ -236,6 +237,7 @@ __device__ __forceinline__ void role_load(const FwdParams& p, uint32_t sbase, ui
   const bool leader = (threadIdx.x & 31u) == 0u;
   uint32_t kv_cnt = 0;
   uint32_t it = 0;
+  if (p.test_flags & 1u) return;  // nothing is loaded: the consumers' bounded waits run out
   for (int w = blockIdx.x; w < p.n_work; w += gridDim.x, ++it) {
     int qp, h, b;
     decode_work(w, p.n_q_pairs, p.n_heads, qp, h, b);

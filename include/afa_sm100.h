@@ -60,7 +60,15 @@ typedef struct AfaFwdArgs {
   float scale;        /* softmax scale; <= 0 selects 1/sqrt(head_dim) as the reference */
   int32_t* status;    /* optional device int32: 0 = ok, else an AFA_DEV_* code (see below) */
   uint64_t timeout_ns; /* bound of every device-side wait; 0 selects the default (4 s) */
+  uint32_t test_flags; /* 0 in normal use; AFA_TEST_* bits below exercise failure paths */
 } AfaFwdArgs;
+
+/* test_flags bit: the kernel's TMA producer issues no loads, so the first
+ * bounded wait of the MMA issuer runs out after timeout_ns.  The kernel then
+ * writes AFA_DEV_TIMEOUT_BASE + site to the status word and returns; nothing is
+ * in flight, the context stays usable.  Lets a test observe the device-side
+ * timeout path without hanging or faulting a GPU. */
+#define AFA_TEST_PRODUCER_IDLE 1u
 
 /*
  * Launch the forward kernel on `stream` (a cudaStream_t) for the current device.
