@@ -2,12 +2,16 @@
 
 Re-exports the sm_100a extension built inside ampere_flash_attention_from_scratch_b200;
 ``forward(kernel_cfg, q, k, v, o, benchmark=False) -> (O, runtime_ms)`` as in the
-reference binding (csrc/ampere_flash_attention.cu:138-141).
+reference binding (csrc/ampere_flash_attention.cu:138-141), plus
+``forward_ext(q, k, v, o=None, causal=False, softmax_scale=None, return_lse=False)
+-> (O, lse)`` for K/V of their own length and head count, the causal mask and
+the log-sum-exp output.
 """
 
 from ampere_flash_attention_from_scratch_b200.afa_flash_attention_kernels import (  # noqa: F401
     _raise_formatted_error,
     check_status,
     forward,
+    forward_ext,
     kernel_keys,
 )

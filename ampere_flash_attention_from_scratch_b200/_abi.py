@@ -60,6 +60,10 @@ class AfaFwdArgs(ctypes.Structure):
         ("status", ctypes.c_void_p),
         ("timeout_ns", ctypes.c_uint64),
         ("test_flags", ctypes.c_uint32),
+        ("seq_len_kv", ctypes.c_int32),
+        ("n_kv_heads", ctypes.c_int32),
+        ("causal", ctypes.c_int32),
+        ("lse", ctypes.c_void_p),
     ]
 
 
@@ -91,8 +95,10 @@ def load() -> ctypes.CDLL:
     return _lib
 
 
-def make_args(q, k, v, o, status=None, scale=0.0, timeout_ns=0, test_flags=0) -> AfaFwdArgs:
-    """AfaFwdArgs for torch tensors q, k, v, o of shape [B, N, H, d] (device memory)."""
+def make_args(q, k, v, o, status=None, scale=0.0, timeout_ns=0, test_flags=0, causal=False,
+              lse=None) -> AfaFwdArgs:
+    """AfaFwdArgs for torch tensors q, o [B, N, H, d] and k, v [B, N_kv, H_kv, d]
+    (device memory); lse: optional fp32 [B, H, N] tensor."""
     dt = {"torch.float16": AFA_DTYPE_FP16, "torch.bfloat16": AFA_DTYPE_BF16}.get(str(q.dtype), -1)
     a = AfaFwdArgs()
     a.q, a.k, a.v, a.o = q.data_ptr(), k.data_ptr(), v.data_ptr(), o.data_ptr()
@@ -104,6 +110,9 @@ def make_args(q, k, v, o, status=None, scale=0.0, timeout_ns=0, test_flags=0) ->
     a.status = status.data_ptr() if status is not None else None
     a.timeout_ns = int(timeout_ns)
     a.test_flags = int(test_flags)
+    a.seq_len_kv, a.n_kv_heads = int(k.shape[1]), int(k.shape[2])
+    a.causal = 1 if causal else 0
+    a.lse = lse.data_ptr() if lse is not None else None
     return a
 
 

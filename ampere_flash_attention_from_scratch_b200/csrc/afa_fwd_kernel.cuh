@@ -1,9 +1,14 @@
 // afa_fwd_kernel.cuh -- Blackwell (sm_100a) FlashAttention forward kernel.
 //
 // Computes O = softmax(Q K^T * scale) V for one (batch, head) slice per work
-// item, non-causal, fp16/bf16 in, fp32 accumulate, fp16/bf16 out.  Same
-// operation as the reference's afa_forward_kernel
-// (csrc/include/afa_forward_kernel.cuh:18-202), re-designed for sm_100a:
+// item, fp16/bf16 in, fp32 accumulate, fp16/bf16 out.  The non-causal,
+// equal-shape case is the reference's afa_forward_kernel
+// (csrc/include/afa_forward_kernel.cuh:18-202); beyond it the kernel takes a
+// key/value length different from the query length, grouped K/V heads (query
+// head h reads K/V head h / kv_group), an optional causal mask aligned to the
+// bottom-right corner (query row i sees keys j <= i + seq_len_kv - seq_len,
+// the FlashAttention convention) and an optional fp32 log-sum-exp output.
+// Re-designed for sm_100a:
 //
 //   * persistent grid (one CTA per SM) walking work items (b, h, q-pair);
 //     a q-pair is 256 query rows = two 128-row Q tiles;
@@ -60,11 +65,15 @@ struct FwdParams {
   unsigned seq_inner_mask;  // bit 0: q, bit 1: k, bit 2: v
   void* o;
   long long o_sb, o_sn, o_sh;  // element strides of O (head_dim stride is 1)
-  int seq_len;
-  int n_heads;
-  int n_q_pairs;  // ceil(seq_len / 256)
-  int n_kv;       // ceil(seq_len / 128)
-  int n_work;     // batch * n_heads * n_q_pairs
+  int seq_len;     // query rows
+  int seq_len_kv;  // key/value rows
+  int n_heads;     // query heads
+  int kv_group;    // query heads per K/V head
+  int n_q_pairs;   // ceil(seq_len / 256)
+  int n_kv;        // ceil(seq_len_kv / 128)
+  int n_work;      // batch * n_heads * n_q_pairs
+  int causal_off;  // seq_len_kv - seq_len: query row i sees keys j <= i + causal_off
+  float* lse;      // optional [batch, n_heads, seq_len] fp32 log-sum-exp (natural log)
   float scale_log2;  // scale * log2(e)
   int* status;
   unsigned long long timeout_ns;
@@ -215,18 +224,36 @@ __device__ __forceinline__ float2 exp2_fma_pipe2(float2 x) {
   return r;
 }
 
-__device__ __forceinline__ void decode_work(int w, int n_q_pairs, int n_heads, int& qp, int& h,
-                                            int& b) {
-  qp = w % n_q_pairs;
-  const int bh = w / n_q_pairs;
-  h = bh % n_heads;
-  b = bh / n_heads;
+// Work item w -> (q-pair, head, batch).  Q-pairs of one head are adjacent in
+// the order, so the CTAs working at one time share the K/V of a few heads in
+// L2.  With a causal mask, q-pairs run from the last (longest) to the first,
+// so the round-robin assignment hands out long items first.
+template <bool kCausal>
+__device__ __forceinline__ void decode_work(const FwdParams& p, int w, int& qp, int& h, int& b) {
+  qp = w % p.n_q_pairs;
+  if (kCausal) qp = p.n_q_pairs - 1 - qp;
+  const int bh = w / p.n_q_pairs;
+  h = bh % p.n_heads;
+  b = bh / p.n_heads;
+}
+
+// K/V tiles that Q tile t (0 or 1) of q-pair qp must visit: all of them, or
+// under the causal mask those up to the last key its last query row sees
+// (at least one, so a tile whose rows see no key still finishes with O = 0).
+// kv_tiles(p, qp, 0) <= kv_tiles(p, qp, 1).
+template <bool kCausal>
+__device__ __forceinline__ int kv_tiles(const FwdParams& p, int qp, int t) {
+  if (!kCausal) return p.n_kv;
+  const int last_row = min(qp * 256 + t * 128 + 127, p.seq_len - 1);
+  const int last_key = last_row + p.causal_off;
+  if (last_key < 0) return 1;
+  return min(last_key / 128 + 1, p.n_kv);
 }
 
 // ---------------------------------------------------------------------------
 // Role: TMA producer (one thread)
 // ---------------------------------------------------------------------------
-template <int kD, bool kBF16, int kStages>
+template <int kD, bool kBF16, int kStages, bool kCausal>
 __device__ __forceinline__ void role_load(const FwdParams& p, uint32_t sbase, uint32_t bar0,
                                           const CtaSync& sy) {
   using L = FwdLayout<kD, kBF16, kStages>;
@@ -240,7 +267,9 @@ __device__ __forceinline__ void role_load(const FwdParams& p, uint32_t sbase, ui
   if (p.test_flags & 1u) return;  // nothing is loaded: the consumers' bounded waits run out
   for (int w = blockIdx.x; w < p.n_work; w += gridDim.x, ++it) {
     int qp, h, b;
-    decode_work(w, p.n_q_pairs, p.n_heads, qp, h, b);
+    decode_work<kCausal>(p, w, qp, h, b);
+    const int h_kv = p.kv_group == 1 ? h : h / p.kv_group;
+    const int n_tiles = kv_tiles<kCausal>(p, qp, 1);
     if (!sy.wait(bar(L::kBarQEmpty), (it & 1u) ^ 1u, kSiteLoadQEmpty)) return;
     if (leader) mbar_arrive_expect_tx(bar(L::kBarQFull), 2u * L::kTileBytes);
 #pragma unroll
@@ -254,7 +283,7 @@ __device__ __forceinline__ void role_load(const FwdParams& p, uint32_t sbase, ui
                       bar(L::kBarQFull), a * 64, si ? row0 : h, si ? h : row0, b, pol_q);
       }
     }
-    for (int j = 0; j < p.n_kv; ++j) {
+    for (int j = 0; j < n_tiles; ++j) {
 #pragma unroll
       for (int kv = 0; kv < 2; ++kv) {
         const uint32_t slot = kv_cnt % kStages;
@@ -268,7 +297,8 @@ __device__ __forceinline__ void role_load(const FwdParams& p, uint32_t sbase, ui
         for (int a = 0; a < L::kAtoms; ++a) {
           if (leader)
             tma_load_4d(sbase + L::kOffKV + slot * L::kTileBytes + a * L::kAtomBytes, map,
-                        bar(L::kBarKVFull + slot), a * 64, si ? row0 : h, si ? h : row0, b, pol_kv);
+                        bar(L::kBarKVFull + slot), a * 64, si ? row0 : h_kv, si ? h_kv : row0, b,
+                        pol_kv);
         }
         ++kv_cnt;
       }
@@ -311,7 +341,7 @@ __device__ __forceinline__ void issue_pv_chunk(uint32_t d_tmem, uint32_t p_tmem,
   }
 }
 
-template <int kD, bool kBF16, int kStages>
+template <int kD, bool kBF16, int kStages, bool kCausal>
 __device__ __forceinline__ void role_mma(const FwdParams& p, uint32_t sbase, uint32_t bar0,
                                          uint32_t tmem, const CtaSync& sy) {
   using L = FwdLayout<kD, kBF16, kStages>;
@@ -338,6 +368,16 @@ __device__ __forceinline__ void role_mma(const FwdParams& p, uint32_t sbase, uin
   };
   bool ok = true;
   for (int w = blockIdx.x; w < p.n_work && ok; w += gridDim.x, ++it) {
+    // Q tile 0 visits n0 K/V tiles, Q tile 1 n1 >= n0 (equal without a causal
+    // mask; the work item is only decoded when they can differ, since this
+    // warp's integer divisions delay the item's first MMA).
+    int n0 = p.n_kv, n1 = p.n_kv;
+    if (kCausal) {
+      int qp, h, b;
+      decode_work<kCausal>(p, w, qp, h, b);
+      n0 = kv_tiles<kCausal>(p, qp, 0);
+      n1 = kv_tiles<kCausal>(p, qp, 1);
+    }
     if (!sy.wait(bar(L::kBarQFull), it & 1u, kSiteMmaQFull)) { ok = false; break; }
     uint32_t ks = kv_cnt % kStages;
     if (!sy.wait(bar(L::kBarKVFull + ks), (kv_cnt / kStages) & 1u, kSiteMmaKFull)) { ok = false; break; }
@@ -349,16 +389,22 @@ __device__ __forceinline__ void role_mma(const FwdParams& p, uint32_t sbase, uin
     umma_commit(bar(L::kBarKVEmpty + ks), leader);
     ++kv_cnt;
     uint32_t vcnt = kv_cnt++;
-    for (int j = 1; j < p.n_kv; ++j) {
+    for (int j = 1; j < n1; ++j) {
       ks = kv_cnt % kStages;
       const uint32_t vs = vcnt % kStages;
       if (!sy.wait(bar(L::kBarKVFull + vs), (vcnt / kStages) & 1u, kSiteMmaVFull)) { ok = false; break; }
       if (!sy.wait(bar(L::kBarKVFull + ks), (kv_cnt / kStages) & 1u, kSiteMmaKFull)) { ok = false; break; }
       // Tensor-core order PV0(j-1), S0(j), PV1(j-1), S1(j): S_i(j) overwrites
       // the TMEM columns P_i(j-1) was read from, after that PV in issue order.
-      if (!pv(0, slot_addr(vs), j > 1)) { ok = false; break; }
-      issue_qk<kD, kBF16, kStages>(tS[0], qa[0], slot_addr(ks), leader);
-      umma_commit(bar(L::kBarSFull + 0), leader);
+      // Q tile 0 stops after n0 tiles (causal): its last PV completes O0.
+      if (j - 1 < n0) {
+        if (!pv(0, slot_addr(vs), j > 1)) { ok = false; break; }
+        if (j == n0) umma_commit(bar(L::kBarOFinal + 0), leader);
+      }
+      if (j < n0) {
+        issue_qk<kD, kBF16, kStages>(tS[0], qa[0], slot_addr(ks), leader);
+        umma_commit(bar(L::kBarSFull + 0), leader);
+      }
       if (!pv(1, slot_addr(vs), j > 1)) { ok = false; break; }
       umma_commit(bar(L::kBarKVEmpty + vs), leader);
       issue_qk<kD, kBF16, kStages>(tS[1], qa[1], slot_addr(ks), leader);
@@ -371,9 +417,11 @@ __device__ __forceinline__ void role_mma(const FwdParams& p, uint32_t sbase, uin
     umma_commit(bar(L::kBarQEmpty), leader);  // all S MMAs of this work item issued: Q may be reloaded
     const uint32_t vs = vcnt % kStages;
     if (!sy.wait(bar(L::kBarKVFull + vs), (vcnt / kStages) & 1u, kSiteMmaVFull)) { ok = false; break; }
-    if (!pv(0, slot_addr(vs), p.n_kv > 1)) { ok = false; break; }
-    umma_commit(bar(L::kBarOFinal + 0), leader);
-    if (!pv(1, slot_addr(vs), p.n_kv > 1)) { ok = false; break; }
+    if (n0 == n1) {
+      if (!pv(0, slot_addr(vs), n1 > 1)) { ok = false; break; }
+      umma_commit(bar(L::kBarOFinal + 0), leader);
+    }
+    if (!pv(1, slot_addr(vs), n1 > 1)) { ok = false; break; }
     umma_commit(bar(L::kBarOFinal + 1), leader);
     umma_commit(bar(L::kBarKVEmpty + vs), leader);
   }
@@ -386,7 +434,7 @@ __device__ __forceinline__ void role_mma(const FwdParams& p, uint32_t sbase, uin
 // ---------------------------------------------------------------------------
 // Role: softmax + correction + epilogue (one warpgroup per Q tile)
 // ---------------------------------------------------------------------------
-template <int kD, bool kBF16, int kStages>
+template <int kD, bool kBF16, int kStages, bool kCausal>
 __device__ __forceinline__ void role_softmax(const FwdParams& p, int wg, uint32_t bar0,
                                              uint32_t tmem, const CtaSync& sy) {
   using L = FwdLayout<kD, kBF16, kStages>;
@@ -406,11 +454,15 @@ __device__ __forceinline__ void role_softmax(const FwdParams& p, int wg, uint32_
 
   for (int w = blockIdx.x; w < p.n_work; w += gridDim.x) {
     int qp, h, b;
-    decode_work(w, p.n_q_pairs, p.n_heads, qp, h, b);
+    decode_work<kCausal>(p, w, qp, h, b);
     const int q_row = qp * 256 + wg * 128 + row;
+    const int n_tiles = kv_tiles<kCausal>(p, qp, wg);
+    // Keys this row sees: all seq_len_kv, or under the causal mask those with
+    // index <= q_row + causal_off.
+    const int row_keys = kCausal ? min(q_row + p.causal_off + 1, p.seq_len_kv) : p.seq_len_kv;
     float m_ref = -INFINITY;  // running reference max, already in log2 units (x scale*log2e)
     float l = 0.f;
-    for (int j = 0; j < p.n_kv; ++j) {
+    for (int j = 0; j < n_tiles; ++j) {
       if (!sy.wait(bar_s, sph, kSiteSoftmaxS)) return;
       sph ^= 1u;
       tc_fence_after_sync();
@@ -420,8 +472,9 @@ __device__ __forceinline__ void role_softmax(const FwdParams& p, int wg, uint32_
       float s[128];
 #pragma unroll
       for (int k = 0; k < 128; ++k) s[k] = __uint_as_float(sr[k]);
-      const int valid = p.seq_len - j * 128;  // key columns of this tile inside the sequence
-      if (valid < 128) {
+      const int valid = row_keys - j * 128;  // key columns of this tile this row sees
+      // Without the causal mask `valid` is the same for every row of the tile.
+      if (kCausal ? __any_sync(0xffffffffu, valid < 128) : valid < 128) {
 #pragma unroll
         for (int k = 0; k < 128; ++k) s[k] = (k < valid) ? s[k] : -INFINITY;
       }
@@ -452,7 +505,10 @@ __device__ __forceinline__ void role_softmax(const FwdParams& p, int wg, uint32_
       }
       if (need) m_ref = m_new;
       const float2 c2 = make_float2(sl2, sl2);
-      const float2 nm2 = make_float2(-m_ref, -m_ref);
+      // A row that has seen no key yet (causal mask) keeps m_ref = -inf; its
+      // masked scores then give exp2(-inf) = 0 instead of exp2(-inf + inf).
+      const float m_use = (kCausal && m_ref == -INFINITY) ? 0.f : m_ref;
+      const float2 nm2 = make_float2(-m_use, -m_use);
       float2 acc0 = make_float2(0.f, 0.f), acc1 = make_float2(0.f, 0.f);
       uint32_t pk[64];
       // P = exp2(S * scale*log2e - m_ref) for one chunk of kSColsPerChunk columns.
@@ -499,12 +555,19 @@ __device__ __forceinline__ void role_softmax(const FwdParams& p, int wg, uint32_
       hand_off(L::kPChunks - 1);
       l = l * alpha + ((acc0.x + acc1.x) + (acc0.y + acc1.y));
     }
-    // Epilogue: O / l, round to the input type, store the row.
+    // Epilogue: O / l, round to the input type, store the row.  A row that
+    // saw no key (causal mask) has l = 0 and O = 0: it stores 0, and a
+    // log-sum-exp of -inf.
     if (!sy.wait(bar_o, oph, kSiteSoftmaxO)) return;
     oph ^= 1u;
     tc_fence_after_sync();
-    const float inv_l = 1.0f / l;
+    const float inv_l = l > 0.f ? 1.0f / l : 0.f;
     const bool row_ok = q_row < p.seq_len;
+    if (p.lse != nullptr && row_ok) {
+      // ln(sum_j exp(s_j * scale)) = (m_ref + log2(l)) * ln(2), m_ref in log2 units.
+      const float lse = l > 0.f ? (m_ref + log2f(l)) * 0.69314718055994531f : -INFINITY;
+      p.lse[(static_cast<long long>(b) * p.n_heads + h) * p.seq_len + q_row] = lse;
+    }
     T* orow = static_cast<T*>(p.o) + static_cast<long long>(b) * p.o_sb +
               static_cast<long long>(q_row) * p.o_sn + static_cast<long long>(h) * p.o_sh;
 #pragma unroll
@@ -529,7 +592,7 @@ __device__ __forceinline__ void role_softmax(const FwdParams& p, int wg, uint32_
 // ---------------------------------------------------------------------------
 // Kernel
 // ---------------------------------------------------------------------------
-template <int kD, bool kBF16, int kStages>
+template <int kD, bool kBF16, int kStages, bool kCausal>
 __global__ void __launch_bounds__(384, 1) afa_fwd_sm100_kernel(const __grid_constant__ FwdParams p) {
   using L = FwdLayout<kD, kBF16, kStages>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
@@ -568,13 +631,13 @@ __global__ void __launch_bounds__(384, 1) afa_fwd_sm100_kernel(const __grid_cons
   if (warp < 4) {
     setmaxnreg_dec<L::kProducerRegs>();
     if (warp == 0) {
-      role_load<kD, kBF16, kStages>(p, sbase, bar0, sy);
+      role_load<kD, kBF16, kStages, kCausal>(p, sbase, bar0, sy);
     } else if (warp == 1) {
-      role_mma<kD, kBF16, kStages>(p, sbase, bar0, tmem, sy);
+      role_mma<kD, kBF16, kStages, kCausal>(p, sbase, bar0, tmem, sy);
     }
   } else {
     setmaxnreg_inc<L::kSoftmaxRegs>();
-    role_softmax<kD, kBF16, kStages>(p, (warp - 4) >> 2, bar0, tmem, sy);
+    role_softmax<kD, kBF16, kStages, kCausal>(p, (warp - 4) >> 2, bar0, tmem, sy);
   }
 
   tc_fence_before_sync();

@@ -18,6 +18,12 @@
 //   * with benchmark=False the returned runtime is 0.0 (the reference returned
 //     an uninitialised float); with benchmark=True the events are destroyed
 //     and the device status word is checked.
+//
+// One function beyond the reference:
+//     O, lse = afa_flash_attention_kernels.forward_ext(q, k, v, o=None, causal=False,
+//                                                      softmax_scale=None, return_lse=False)
+// with K/V of their own length and head count (GQA), the causal mask and the
+// fp32 log-sum-exp [batch, heads, seq] (None unless return_lse).
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <cuda_runtime.h>
@@ -82,6 +88,9 @@ int32_t read_and_clear_status(const at::Device& dev) {
   return v;
 }
 
+float launch(const at::Tensor& TQ, const at::Tensor& TK, const at::Tensor& TV, const at::Tensor& TO,
+             int dt, float scale, bool causal, float* lse, bool benchmark);
+
 std::tuple<at::Tensor, double> flash_attention_forward(const py::object& py_cfg,
                                                        const at::Tensor& TQ, const at::Tensor& TK,
                                                        const at::Tensor& TV,
@@ -137,6 +146,15 @@ std::tuple<at::Tensor, double> flash_attention_forward(const py::object& py_cfg,
     TO = at::empty_like(TQ, at::MemoryFormat::Contiguous);
   }
 
+  const float runtime = launch(TQ, TK, TV, TO, dt, 0.f /* 1/sqrt(d_head), as the reference */,
+                               false, nullptr, benchmark);
+  return std::make_tuple(TO, static_cast<double>(runtime));
+}
+
+// Fills AfaFwdArgs from the tensors and launches on the current stream; with
+// `benchmark`, times the launch with CUDA events and checks the status word.
+float launch(const at::Tensor& TQ, const at::Tensor& TK, const at::Tensor& TV, const at::Tensor& TO,
+             int dt, float scale, bool causal, float* lse, bool benchmark) {
   AfaFwdArgs args{};
   args.q = TQ.data_ptr();
   args.k = TK.data_ptr();
@@ -151,10 +169,14 @@ std::tuple<at::Tensor, double> flash_attention_forward(const py::object& py_cfg,
   args.n_heads = static_cast<int32_t>(TQ.size(2));
   args.head_dim = static_cast<int32_t>(TQ.size(3));
   args.dtype = dt;
-  args.scale = 0.f;  // 1/sqrt(d_head), fixed as in the reference kernel
+  args.scale = scale;
   at::Tensor& status = status_word(TQ.device());
   args.status = status.data_ptr<int32_t>();
   args.timeout_ns = 0;
+  args.seq_len_kv = static_cast<int32_t>(TK.size(1));
+  args.n_kv_heads = static_cast<int32_t>(TK.size(2));
+  args.causal = causal ? 1 : 0;
+  args.lse = lse;
 
   cudaStream_t stream = at::cuda::getCurrentCUDAStream().stream();
   float runtime = 0.f;
@@ -177,7 +199,70 @@ std::tuple<at::Tensor, double> flash_attention_forward(const py::object& py_cfg,
     const int32_t st = read_and_clear_status(TQ.device());
     TORCH_CHECK(st == 0, "attention kernel reported: ", afa_status_string(st));
   }
-  return std::make_tuple(TO, static_cast<double>(runtime));
+  return runtime;
+}
+
+// Beyond the reference: q [B, N, H, d]; k, v [B, N_kv, H_kv, d] with H_kv
+// dividing H; optional causal mask (bottom-right aligned); optional fp32
+// log-sum-exp [B, H, N].  Returns (O, lse or None).
+std::tuple<at::Tensor, std::optional<at::Tensor>> forward_ext(
+    const at::Tensor& TQ, const at::Tensor& TK, const at::Tensor& TV, std::optional<at::Tensor> out_,
+    bool causal, std::optional<double> softmax_scale, bool return_lse) {
+  AFA_CHECK_CUDA(TQ);
+  AFA_CHECK_CUDA(TK);
+  AFA_CHECK_CUDA(TV);
+  AFA_CHECK_LAST_DIM(TQ);
+  AFA_CHECK_LAST_DIM(TK);
+  AFA_CHECK_LAST_DIM(TV);
+  c10::cuda::CUDAGuard device_guard{TQ.device()};
+  const int dev = TQ.device().index();
+  int major = 0, minor = 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+  TORCH_CHECK(major == 10 && minor == 0,
+              "Flash Attention (sm_100a build) requires SM_100 (current: SM_", major, ".", minor,
+              ")");
+  const int dt = dtype_code(TQ);
+  TORCH_CHECK(dt > 0, "Only fp16 and bf16 are supported");
+  TORCH_CHECK(TK.dtype() == TQ.dtype() && TV.dtype() == TQ.dtype(),
+              "Input tensors must have the same data type");
+  TORCH_CHECK(TK.device() == TQ.device() && TV.device() == TQ.device(),
+              "Input tensors must be on the same device");
+  TORCH_CHECK(afa_fwd_sm100_supported(dt, static_cast<int32_t>(TQ.size(3))) == 1,
+              "no sm_100a kernel for head_dim ", TQ.size(3), " (64 and 128 are compiled)");
+  TORCH_CHECK(TK.sizes() == TV.sizes(), "key and value tensors must have the same shape");
+  TORCH_CHECK(TK.size(0) == TQ.size(0), "query and key batch sizes differ");
+  TORCH_CHECK(TK.size(3) == TQ.size(3), "query and key head_dim differ");
+  TORCH_CHECK(TQ.size(0) > 0 && TQ.size(1) > 0 && TQ.size(2) > 0 && TK.size(1) > 0 && TK.size(2) > 0,
+              "batch, seq_len and n_heads must be positive");
+  TORCH_CHECK(TQ.size(2) % TK.size(2) == 0, "the number of query heads (", TQ.size(2),
+              ") must be a multiple of the number of key/value heads (", TK.size(2), ")");
+  TORCH_CHECK(TQ.size(0) <= INT32_MAX && TQ.size(1) <= INT32_MAX && TQ.size(2) <= INT32_MAX &&
+                  TK.size(1) <= INT32_MAX,
+              "tensor dimension too large");
+  double scale = 0.0;
+  if (softmax_scale.has_value()) {
+    scale = softmax_scale.value();
+    TORCH_CHECK(scale > 0.0, "softmax_scale must be positive");
+  }
+  at::Tensor TO;
+  if (out_.has_value() && out_->defined()) {
+    TO = out_.value();
+    AFA_CHECK_CUDA(TO);
+    AFA_CHECK_LAST_DIM(TO);
+    TORCH_CHECK(TO.dtype() == TQ.dtype(), "Output tensor must have the same dtype as inputs");
+    TORCH_CHECK(TQ.sizes() == TO.sizes(), "Query and output tensors have same shape");
+    TORCH_CHECK(TO.device() == TQ.device(), "Output tensor must be on the same device");
+  } else {
+    TO = at::empty_like(TQ, at::MemoryFormat::Contiguous);
+  }
+  std::optional<at::Tensor> lse;
+  if (return_lse)
+    lse = at::empty({TQ.size(0), TQ.size(2), TQ.size(1)},
+                    at::TensorOptions().dtype(at::kFloat).device(TQ.device()));
+  launch(TQ, TK, TV, TO, dt, static_cast<float>(scale), causal,
+         lse.has_value() ? lse->data_ptr<float>() : nullptr, false);
+  return std::make_tuple(TO, lse);
 }
 
 // Reads (and clears) the device status word of `device`; raises RuntimeError
@@ -210,6 +295,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("forward", &flash_attention_forward, py::arg("kernel_cfg"), py::arg("q"), py::arg("k"),
         py::arg("v"), py::arg("o") = py::none(), py::arg("benchmark") = false,
         "Flash Attention forward (CUDA, sm_100a)");
+  m.def("forward_ext", &forward_ext, py::arg("q"), py::arg("k"), py::arg("v"),
+        py::arg("o") = py::none(), py::arg("causal") = false, py::arg("softmax_scale") = py::none(),
+        py::arg("return_lse") = false,
+        "Attention forward with K/V of their own length and head count (GQA), an optional causal "
+        "mask (bottom-right aligned) and an optional fp32 log-sum-exp [batch, heads, seq]");
   m.def("check_status", &check_status, py::arg("device") = 0,
         "Raise RuntimeError if a kernel on `device` reported an error since the last check");
   m.def("_raise_formatted_error", &raise_formatted_error, py::arg("a"), py::arg("b"));

@@ -2,10 +2,13 @@
  * afa_sm100.h -- C ABI of the B200 (sm_100a) attention-forward library
  * (libafa_sm100.so).
  *
- * Computes the non-causal attention forward  O = softmax(Q K^T * scale) V  for
- * fp16/bf16 tensors laid out as [batch, seq_len, n_heads, head_dim], the same
- * operation and layout as the reference's torch binding
- * `afa_flash_attention_kernels.forward` (csrc/ampere_flash_attention.cu:35-136).
+ * Computes the attention forward  O = softmax(Q K^T * scale) V  for fp16/bf16
+ * tensors laid out as [batch, seq_len, n_heads, head_dim].  With the extension
+ * fields of AfaFwdArgs left zero it is exactly the operation and layout of the
+ * reference's torch binding `afa_flash_attention_kernels.forward`
+ * (csrc/ampere_flash_attention.cu:35-136): non-causal, K and V shaped like Q.
+ * The extensions add a K/V length different from the query length, grouped
+ * K/V heads (GQA), a causal mask and a log-sum-exp output.
  *
  * Plain C types only: pointers are device addresses, the stream is a
  * cudaStream_t passed as void*.  No call allocates, frees or synchronizes; all
@@ -28,7 +31,7 @@ extern "C" {
 
 /* Return codes. */
 #define AFA_OK 0
-#define AFA_ERR_INVALID_ARGUMENT 1   /* null pointer, non-positive size, bad stride */
+#define AFA_ERR_INVALID_ARGUMENT 1   /* null pointer, non-positive size, n_kv_heads not dividing n_heads, causal not 0/1 */
 #define AFA_ERR_UNSUPPORTED_DTYPE 2  /* dtype not fp16/bf16 */
 #define AFA_ERR_NO_KERNEL 3          /* no compiled kernel for (dtype, head_dim) */
 #define AFA_ERR_MISALIGNED 4         /* base address / stride not 16-byte aligned */
@@ -41,8 +44,10 @@ extern "C" {
 
 /* Arguments of one forward call.  Strides are in elements, for the
  * (batch, seq, head) dimensions; head_dim must be contiguous (stride 1).
+ * Q and O are [batch, seq_len, n_heads, head_dim]; K and V are
+ * [batch, seq_len_kv, n_kv_heads, head_dim].
  * Replaces the reference's AFAForwardParams (csrc/include/afa_config.cuh:7-34),
- * which had one stride set shared by all four tensors. */
+ * which had one stride set shared by all four tensors and one shape. */
 typedef struct AfaFwdArgs {
   const void* q;
   const void* k;
@@ -61,6 +66,16 @@ typedef struct AfaFwdArgs {
   int32_t* status;    /* optional device int32: 0 = ok, else an AFA_DEV_* code (see below) */
   uint64_t timeout_ns; /* bound of every device-side wait; 0 selects the default (4 s) */
   uint32_t test_flags; /* 0 in normal use; AFA_TEST_* bits below exercise failure paths */
+  /* Extensions (ABI 2.0); zero everywhere gives the reference's operation. */
+  int32_t seq_len_kv;  /* rows of K and V; 0 selects seq_len */
+  int32_t n_kv_heads;  /* heads of K and V, a divisor of n_heads (query head h reads
+                          K/V head h / (n_heads / n_kv_heads)); 0 selects n_heads */
+  int32_t causal;      /* 1: query row i sees only keys j <= i + seq_len_kv - seq_len
+                          (bottom-right aligned, the FlashAttention convention); a row
+                          that sees no key gets O = 0.  0: no mask */
+  float* lse;          /* optional device fp32 [batch, n_heads, seq_len], contiguous:
+                          ln(sum_j exp(scale * q_i . k_j)) over the keys row i sees,
+                          -inf for a row that sees none.  NULL: not written */
 } AfaFwdArgs;
 
 /* test_flags bit: the kernel's TMA producer issues no loads, so the first

@@ -10,6 +10,13 @@ per (batch, head) slice, non-causal, no dropout, scale = 1/sqrt(d_head)
 (csrc/include/afa_forward_kernel.cuh:83-84 folds log2(e) into that scale and
 uses exp2; mathematically the same softmax).  Layout [B, N, H, d].
 
+Beyond the reference (which has neither), ``attention_fp32`` and
+``attention_fp64`` also take K/V with their own length and head count
+(query head h reads K/V head h // (H // H_kv)), a causal mask aligned to the
+bottom-right corner (query row i sees keys j <= i + N_kv - N; a row that sees
+no key gives O = 0 and log-sum-exp -inf) and return the log-sum-exp
+ln(sum_j exp(scale * q_i . k_j)) per row on request.
+
 Three forms:
 * ``attention_fp32``       -- fp32 math on the (fp16/bf16-valued) inputs, the
   "naive torch fp32 softmax(QK^T*scale)V" oracle named by the north star; also
@@ -46,47 +53,73 @@ def default_scale(d_head: int) -> float:
 
 
 def attention_fp32(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, scale: float | None = None,
-                   slices=None, max_scores: int = 1 << 26) -> torch.Tensor:
+                   slices=None, max_scores: int = 1 << 26, causal: bool = False,
+                   return_lse: bool = False):
     """fp32 softmax(Q K^T * scale) V on CPU (or wherever the inputs live).
 
-    q, k, v: [B, N, H, d] of any float dtype; values are taken exactly and the
-    arithmetic is fp32.  ``slices``: optional list of (b, h) pairs; when given,
-    returns [len(slices), N, d] for those slices only.  Otherwise returns
-    [B, N, H, d] fp32.  Rows are processed in chunks so at most ``max_scores``
-    fp32 scores exist at once.
+    q: [B, N, H, d]; k, v: [B, N_kv, H_kv, d] (H_kv divides H) of any float
+    dtype; values are taken exactly and the arithmetic is fp32.  ``slices``:
+    optional list of (b, h) pairs; when given, returns [len(slices), N, d] for
+    those slices only.  Otherwise returns [B, N, H, d] fp32.  Rows are
+    processed in chunks so at most ``max_scores`` fp32 scores exist at once.
+    With ``return_lse`` also returns the fp32 log-sum-exp, [B, H, N] (or
+    [len(slices), N]).
     """
     B, N, H, d = q.shape
+    n_kv, h_kv = k.shape[1], k.shape[2]
+    group = H // h_kv
     if scale is None:
         scale = default_scale(d)
     pairs = slices if slices is not None else [(b, h) for b in range(B) for h in range(H)]
     out = torch.empty((len(pairs), N, d), dtype=torch.float32, device=q.device)
-    rows = max(1, min(N, max_scores // max(N, 1)))
+    lse = torch.empty((len(pairs), N), dtype=torch.float32, device=q.device)
+    rows = max(1, min(N, max_scores // max(n_kv, 1)))
+    off = n_kv - N
+    keys = torch.arange(n_kv, device=q.device)
     for i, (b, h) in enumerate(pairs):
         qs = q[b, :, h, :].float()
-        ks = k[b, :, h, :].float()
-        vs = v[b, :, h, :].float()
+        ks = k[b, :, h // group, :].float()
+        vs = v[b, :, h // group, :].float()
         for r0 in range(0, N, rows):
             s = (qs[r0:r0 + rows] @ ks.t()) * scale
-            s = s - s.amax(dim=-1, keepdim=True)
-            p = torch.exp(s)
-            out[i, r0:r0 + rows] = (p @ vs) / p.sum(dim=-1, keepdim=True)
+            if causal:
+                r = torch.arange(r0, min(r0 + rows, N), device=q.device)
+                s = s.masked_fill(keys[None, :] > (r[:, None] + off), float("-inf"))
+            m = s.amax(dim=-1, keepdim=True)
+            m = torch.where(torch.isinf(m), torch.zeros_like(m), m)  # rows that see no key
+            p = torch.exp(s - m)
+            l = p.sum(dim=-1, keepdim=True)
+            out[i, r0:r0 + rows] = torch.where(l > 0, (p @ vs) / l, torch.zeros_like(l))
+            lse[i, r0:r0 + rows] = (m + torch.log(l)).squeeze(-1)
     if slices is not None:
-        return out
-    return out.view(B, H, N, d).permute(0, 2, 1, 3).contiguous()
+        return (out, lse) if return_lse else out
+    o = out.view(B, H, N, d).permute(0, 2, 1, 3).contiguous()
+    return (o, lse.view(B, H, N)) if return_lse else o
 
 
-def attention_fp64(q, k, v, scale: float | None = None) -> np.ndarray:
-    """float64 numpy softmax(Q K^T * scale) V; q, k, v [B, N, H, d] (torch or numpy)."""
+def attention_fp64(q, k, v, scale: float | None = None, causal: bool = False, return_lse: bool = False):
+    """float64 numpy softmax(Q K^T * scale) V; q [B, N, H, d], k, v [B, N_kv, H_kv, d]
+    (torch or numpy).  Same mask and log-sum-exp conventions as attention_fp32."""
     qn, kn, vn = (np.asarray(t.float().cpu().numpy() if isinstance(t, torch.Tensor) else t, dtype=np.float64)
                   for t in (q, k, v))
-    d = qn.shape[-1]
+    B, N, H, d = qn.shape
+    n_kv, h_kv = kn.shape[1], kn.shape[2]
+    kn = np.repeat(kn, H // h_kv, axis=2)
+    vn = np.repeat(vn, H // h_kv, axis=2)
     if scale is None:
         scale = default_scale(d)
     s = np.einsum("bnhd,bmhd->bhnm", qn, kn) * scale
-    s -= s.max(axis=-1, keepdims=True)
-    p = np.exp(s)
-    p /= p.sum(axis=-1, keepdims=True)
-    return np.einsum("bhnm,bmhd->bnhd", p, vn)
+    if causal:
+        mask = np.arange(n_kv)[None, :] > (np.arange(N)[:, None] + (n_kv - N))
+        s = np.where(mask[None, None], -np.inf, s)
+    m = s.max(axis=-1, keepdims=True)
+    m = np.where(np.isinf(m), 0.0, m)
+    p = np.exp(s - m)
+    l = p.sum(axis=-1, keepdims=True)
+    with np.errstate(invalid="ignore", divide="ignore"):
+        o = np.einsum("bhnm,bmhd->bnhd", np.where(l > 0, p / l, 0.0), vn)
+        lse = (m + np.log(l))[..., 0]
+    return (o, lse) if return_lse else o
 
 
 def _round_to(x: np.ndarray, torch_dtype) -> np.ndarray:

@@ -82,6 +82,13 @@ def valid_args(**over):
         ({"n_heads": 0}, _abi.AFA_ERR_INVALID_ARGUMENT),
         ({"k": 0x100008}, _abi.AFA_ERR_MISALIGNED),
         ({"batch": 1 << 20, "n_heads": 1 << 10, "seq_len": 1 << 20}, _abi.AFA_ERR_TOO_LARGE),
+        # extension fields
+        ({"n_kv_heads": 3}, _abi.AFA_ERR_INVALID_ARGUMENT),  # does not divide n_heads = 4
+        ({"n_kv_heads": -1}, _abi.AFA_ERR_INVALID_ARGUMENT),
+        ({"seq_len_kv": -5}, _abi.AFA_ERR_INVALID_ARGUMENT),
+        ({"causal": 2}, _abi.AFA_ERR_INVALID_ARGUMENT),
+        ({"lse": 0x100002}, _abi.AFA_ERR_MISALIGNED),
+        ({"seq_len_kv": (1 << 31) - 100}, _abi.AFA_ERR_TOO_LARGE),
     ],
 )
 def test_argument_errors_without_gpu(over, code):
@@ -100,6 +107,18 @@ def test_misaligned_stride_rejected():
     assert rc != _abi.AFA_ERR_MISALIGNED
 
 
+def test_kv_strides_checked_against_kv_shape():
+    lib = _abi.load()
+    # K/V with one head (GQA): the K head stride is never used, so any value passes
+    # the alignment check; a bad K seq stride is still caught.
+    a = valid_args(n_kv_heads=1, seq_len_kv=300)
+    a.k_strides[:] = [300 * 128, 128, 3]
+    a.v_strides[:] = [300 * 128, 128, 3]
+    assert lib.afa_fwd_sm100(ctypes.byref(a), None) not in (_abi.AFA_ERR_MISALIGNED, _abi.AFA_ERR_INVALID_ARGUMENT)
+    a.k_strides[1] = 130
+    assert lib.afa_fwd_sm100(ctypes.byref(a), None) == _abi.AFA_ERR_MISALIGNED
+
+
 def test_null_args_pointer():
     assert _abi.load().afa_fwd_sm100(None, None) == _abi.AFA_ERR_INVALID_ARGUMENT
 
@@ -116,4 +135,4 @@ def test_strings_and_queries():
     assert 0 < lib.afa_fwd_sm100_smem_bytes(5, 128) <= 232448
     assert lib.afa_fwd_sm100_smem_bytes(5, 96) == -1
     assert lib.afa_fwd_sm100_threads() == 384
-    assert lib.afa_sm100_version() >= 100
+    assert lib.afa_sm100_version() >= 200
