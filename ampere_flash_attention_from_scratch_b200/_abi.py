@@ -28,6 +28,7 @@ AFA_ERR_DEVICE_TIMEOUT = 9
 AFA_ERR_TOO_LARGE = 10
 AFA_DEV_TIMEOUT_BASE = 0x100
 AFA_TEST_PRODUCER_IDLE = 1
+AFA_TEST_MMA_IDLE = 2
 
 # Every extern "C" symbol declared in include/afa_sm100.h.
 EXPORTED_SYMBOLS = (

@@ -36,7 +36,8 @@
 //
 // Every mbarrier wait is bounded (globaltimer deadline): on expiry the kernel
 // records AFA_DEV_TIMEOUT_BASE + site in the status word, raises a CTA-wide
-// abort flag and every role returns, so a bug cannot hang the GPU.
+// abort flag and every role returns (the producer first waits, bounded, for
+// the loads it still has in flight), so a bug cannot hang the GPU.
 #pragma once
 
 #include <cstdint>
@@ -77,7 +78,8 @@ struct FwdParams {
   float scale_log2;  // scale * log2(e)
   int* status;
   unsigned long long timeout_ns;
-  unsigned test_flags;  // bit 0: the producer issues no loads (exercises the timeout path)
+  unsigned test_flags;  // bit 0: the producer issues no loads; bit 1: the MMA issuer issues nothing
+                        // (both exercise the timeout path; bit 1 with loads in flight)
 };
 
 // Bounded-wait sites, reported as AFA_DEV_TIMEOUT_BASE + site.
@@ -262,15 +264,16 @@ __device__ __forceinline__ void role_load(const FwdParams& p, uint32_t sbase, ui
   const uint64_t pol_q = l2_policy_evict_first();
   // The whole warp runs this role in converged control flow; lane 0 issues.
   const bool leader = (threadIdx.x & 31u) == 0u;
-  uint32_t kv_cnt = 0;
+  uint32_t kv_cnt = 0, q_cnt = 0;
   uint32_t it = 0;
+  bool ok = true;
   if (p.test_flags & 1u) return;  // nothing is loaded: the consumers' bounded waits run out
-  for (int w = blockIdx.x; w < p.n_work; w += gridDim.x, ++it) {
+  for (int w = blockIdx.x; w < p.n_work && ok; w += gridDim.x, ++it) {
     int qp, h, b;
     decode_work<kCausal>(p, w, qp, h, b);
     const int h_kv = p.kv_group == 1 ? h : h / p.kv_group;
     const int n_tiles = kv_tiles<kCausal>(p, qp, 1);
-    if (!sy.wait(bar(L::kBarQEmpty), (it & 1u) ^ 1u, kSiteLoadQEmpty)) return;
+    if (!sy.wait(bar(L::kBarQEmpty), (it & 1u) ^ 1u, kSiteLoadQEmpty)) { ok = false; break; }
     if (leader) mbar_arrive_expect_tx(bar(L::kBarQFull), 2u * L::kTileBytes);
 #pragma unroll
     for (int t = 0; t < 2; ++t) {
@@ -283,12 +286,13 @@ __device__ __forceinline__ void role_load(const FwdParams& p, uint32_t sbase, ui
                       bar(L::kBarQFull), a * 64, si ? row0 : h, si ? h : row0, b, pol_q);
       }
     }
-    for (int j = 0; j < n_tiles; ++j) {
+    ++q_cnt;
+    for (int j = 0; j < n_tiles && ok; ++j) {
 #pragma unroll
       for (int kv = 0; kv < 2; ++kv) {
         const uint32_t slot = kv_cnt % kStages;
         const uint32_t ph = (kv_cnt / kStages) & 1u;
-        if (!sy.wait(bar(L::kBarKVEmpty + slot), ph ^ 1u, kSiteLoadKVEmpty)) return;
+        if (!sy.wait(bar(L::kBarKVEmpty + slot), ph ^ 1u, kSiteLoadKVEmpty)) { ok = false; break; }
         if (leader) mbar_arrive_expect_tx(bar(L::kBarKVFull + slot), L::kTileBytes);
         const CUtensorMap* map = kv ? &p.tm_v : &p.tm_k;
         const bool si = (p.seq_inner_mask & (kv ? 4u : 2u)) != 0u;
@@ -304,6 +308,18 @@ __device__ __forceinline__ void role_load(const FwdParams& p, uint32_t sbase, ui
       }
     }
   }
+  if (ok) return;
+  // Aborted: before the CTA may exit, wait (bounded, not cut short by the
+  // abort flag) until the loads still in flight have landed -- the last
+  // kStages K/V loads and the last Q load.  Phases that already completed
+  // return at once.
+  const uint32_t first = kv_cnt > static_cast<uint32_t>(kStages) ? kv_cnt - kStages : 0u;
+  for (uint32_t n = first; n < kv_cnt; ++n) {
+    const uint32_t fb = bar(L::kBarKVFull + static_cast<int>(n % kStages));
+    if (!mbar_try_wait(fb, (n / kStages) & 1u)) sy.wait_slow(fb, (n / kStages) & 1u, kSiteLoadKVEmpty, false);
+  }
+  if (q_cnt > 0 && !mbar_try_wait(bar(L::kBarQFull), (q_cnt - 1u) & 1u))
+    sy.wait_slow(bar(L::kBarQFull), (q_cnt - 1u) & 1u, kSiteLoadQEmpty, false);
 }
 
 // ---------------------------------------------------------------------------
@@ -366,7 +382,7 @@ __device__ __forceinline__ void role_mma(const FwdParams& p, uint32_t sbase, uin
     pph[wg] ^= 1u;
     return true;
   };
-  bool ok = true;
+  bool ok = (p.test_flags & 2u) == 0u;  // bit 1: issue nothing; the other roles' waits run out
   for (int w = blockIdx.x; w < p.n_work && ok; w += gridDim.x, ++it) {
     // Q tile 0 visits n0 K/V tiles, Q tile 1 n1 >= n0 (equal without a causal
     // mask; the work item is only decoded when they can differ, since this

@@ -84,6 +84,12 @@ typedef struct AfaFwdArgs {
  * in flight, the context stays usable.  Lets a test observe the device-side
  * timeout path without hanging or faulting a GPU. */
 #define AFA_TEST_PRODUCER_IDLE 1u
+/* test_flags bit: the MMA issuer issues nothing, so the producer fills the
+ * K/V ring and its bounded wait for a free slot runs out while its loads have
+ * landed or are landing: it waits (bounded) for them before the CTA exits, and
+ * the softmax warps' waits for S run out too.  Status word and context as for
+ * AFA_TEST_PRODUCER_IDLE. */
+#define AFA_TEST_MMA_IDLE 2u
 
 /*
  * Launch the forward kernel on `stream` (a cudaStream_t) for the current device.

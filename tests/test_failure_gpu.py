@@ -4,7 +4,10 @@ With AFA_TEST_PRODUCER_IDLE the kernel's TMA producer loads nothing, so the
 MMA issuer's bounded wait for Q runs out after a short timeout_ns: the kernel
 must report AFA_DEV_TIMEOUT_BASE + site in the status word and return (no hang,
 no fault, nothing left in flight), and the next normal call on the same
-context must still produce the right answer.
+context must still produce the right answer.  With AFA_TEST_MMA_IDLE the MMA
+issuer issues nothing: the producer fills the K/V ring, its wait for a free
+slot runs out with its loads in flight or landed, and it waits for them before
+the CTA exits -- same checks.
 """
 
 import ctypes
@@ -18,7 +21,8 @@ from oracle.attention_oracle import attention_fp32, error_stats
 pytestmark = pytest.mark.gpu
 
 
-def test_bounded_wait_runs_out_and_context_survives():
+@pytest.mark.parametrize("flag", [_abi.AFA_TEST_PRODUCER_IDLE, _abi.AFA_TEST_MMA_IDLE])
+def test_bounded_wait_runs_out_and_context_survives(flag):
     lib = _abi.load()
     dev = torch.device("cuda:0")
     g = torch.Generator().manual_seed(5)
@@ -29,7 +33,7 @@ def test_bounded_wait_runs_out_and_context_survives():
     stream = torch.cuda.current_stream().cuda_stream
 
     a = _abi.make_args(qd, kd, vd, o, status=status, timeout_ns=20_000_000,
-                       test_flags=_abi.AFA_TEST_PRODUCER_IDLE)
+                       test_flags=flag)
     assert lib.afa_fwd_sm100(ctypes.byref(a), stream) == _abi.AFA_OK
     torch.cuda.synchronize()
     st = int(status.item())
