@@ -109,11 +109,13 @@ struct FwdLayout {
   static constexpr uint32_t kOffKV = 2 * kTileBytes;
   static constexpr uint32_t kOffBar = kOffKV + kStages * kTileBytes;
   // mbarrier indices
-  static constexpr int kBarQFull = 0;
-  static constexpr int kBarQEmpty = 1;
-  static constexpr int kBarKVFull = 2;                   // [kStages]
-  static constexpr int kBarKVEmpty = 2 + kStages;        // [kStages]
-  static constexpr int kBarSFull = 2 + 2 * kStages;      // [2]
+  // Each Q tile has its own full/empty pair, so the next work item's Q0 loads
+  // as soon as the current item's last S0 is issued.
+  static constexpr int kBarQFull = 0;                    // [2]
+  static constexpr int kBarQEmpty = 2;                   // [2]
+  static constexpr int kBarKVFull = 4;                   // [kStages]
+  static constexpr int kBarKVEmpty = 4 + kStages;        // [kStages]
+  static constexpr int kBarSFull = 4 + 2 * kStages;      // [2]
   // P is handed to the PV MMA in kPChunks column chunks, one barrier each, so
   // the tensor core starts O += P V on the first chunk while the softmax
   // warpgroup is still computing the rest.
@@ -264,7 +266,7 @@ __device__ __forceinline__ void role_load(const FwdParams& p, uint32_t sbase, ui
   const uint64_t pol_q = l2_policy_evict_first();
   // The whole warp runs this role in converged control flow; lane 0 issues.
   const bool leader = (threadIdx.x & 31u) == 0u;
-  uint32_t kv_cnt = 0, q_cnt = 0;
+  uint32_t kv_cnt = 0, q_cnt[2] = {0u, 0u};
   uint32_t it = 0;
   bool ok = true;
   if (p.test_flags & 1u) return;  // nothing is loaded: the consumers' bounded waits run out
@@ -273,20 +275,21 @@ __device__ __forceinline__ void role_load(const FwdParams& p, uint32_t sbase, ui
     decode_work<kCausal>(p, w, qp, h, b);
     const int h_kv = p.kv_group == 1 ? h : h / p.kv_group;
     const int n_tiles = kv_tiles<kCausal>(p, qp, 1);
-    if (!sy.wait(bar(L::kBarQEmpty), (it & 1u) ^ 1u, kSiteLoadQEmpty)) { ok = false; break; }
-    if (leader) mbar_arrive_expect_tx(bar(L::kBarQFull), 2u * L::kTileBytes);
 #pragma unroll
     for (int t = 0; t < 2; ++t) {
+      if (!sy.wait(bar(L::kBarQEmpty + t), (it & 1u) ^ 1u, kSiteLoadQEmpty)) { ok = false; break; }
+      if (leader) mbar_arrive_expect_tx(bar(L::kBarQFull + t), L::kTileBytes);
 #pragma unroll
       for (int a = 0; a < L::kAtoms; ++a) {
         const int row0 = qp * 256 + t * 128;
         const bool si = (p.seq_inner_mask & 1u) != 0u;
         if (leader)
           tma_load_4d(sbase + L::kOffQ + t * L::kTileBytes + a * L::kAtomBytes, &p.tm_q,
-                      bar(L::kBarQFull), a * 64, si ? row0 : h, si ? h : row0, b, pol_q);
+                      bar(L::kBarQFull + t), a * 64, si ? row0 : h, si ? h : row0, b, pol_q);
       }
+      ++q_cnt[t];
     }
-    ++q_cnt;
+    if (!ok) break;
     for (int j = 0; j < n_tiles && ok; ++j) {
 #pragma unroll
       for (int kv = 0; kv < 2; ++kv) {
@@ -318,8 +321,9 @@ __device__ __forceinline__ void role_load(const FwdParams& p, uint32_t sbase, ui
     const uint32_t fb = bar(L::kBarKVFull + static_cast<int>(n % kStages));
     if (!mbar_try_wait(fb, (n / kStages) & 1u)) sy.wait_slow(fb, (n / kStages) & 1u, kSiteLoadKVEmpty, false);
   }
-  if (q_cnt > 0 && !mbar_try_wait(bar(L::kBarQFull), (q_cnt - 1u) & 1u))
-    sy.wait_slow(bar(L::kBarQFull), (q_cnt - 1u) & 1u, kSiteLoadQEmpty, false);
+  for (int t = 0; t < 2; ++t)
+    if (q_cnt[t] > 0 && !mbar_try_wait(bar(L::kBarQFull + t), (q_cnt[t] - 1u) & 1u))
+      sy.wait_slow(bar(L::kBarQFull + t), (q_cnt[t] - 1u) & 1u, kSiteLoadQEmpty, false);
 }
 
 // ---------------------------------------------------------------------------
@@ -394,12 +398,15 @@ __device__ __forceinline__ void role_mma(const FwdParams& p, uint32_t sbase, uin
       n0 = kv_tiles<kCausal>(p, qp, 0);
       n1 = kv_tiles<kCausal>(p, qp, 1);
     }
-    if (!sy.wait(bar(L::kBarQFull), it & 1u, kSiteMmaQFull)) { ok = false; break; }
+    if (!sy.wait(bar(L::kBarQFull + 0), it & 1u, kSiteMmaQFull)) { ok = false; break; }
     uint32_t ks = kv_cnt % kStages;
     if (!sy.wait(bar(L::kBarKVFull + ks), (kv_cnt / kStages) & 1u, kSiteMmaKFull)) { ok = false; break; }
     tc_fence_after_sync();
     issue_qk<kD, kBF16, kStages>(tS[0], qa[0], slot_addr(ks), leader);
     umma_commit(bar(L::kBarSFull + 0), leader);
+    if (n0 == 1) umma_commit(bar(L::kBarQEmpty + 0), leader);  // last S0 of the item issued
+    if (!sy.wait(bar(L::kBarQFull + 1), it & 1u, kSiteMmaQFull)) { ok = false; break; }
+    tc_fence_after_sync();
     issue_qk<kD, kBF16, kStages>(tS[1], qa[1], slot_addr(ks), leader);
     umma_commit(bar(L::kBarSFull + 1), leader);
     umma_commit(bar(L::kBarKVEmpty + ks), leader);
@@ -420,6 +427,7 @@ __device__ __forceinline__ void role_mma(const FwdParams& p, uint32_t sbase, uin
       if (j < n0) {
         issue_qk<kD, kBF16, kStages>(tS[0], qa[0], slot_addr(ks), leader);
         umma_commit(bar(L::kBarSFull + 0), leader);
+        if (j == n0 - 1) umma_commit(bar(L::kBarQEmpty + 0), leader);  // last S0 of the item
       }
       if (!pv(1, slot_addr(vs), j > 1)) { ok = false; break; }
       umma_commit(bar(L::kBarKVEmpty + vs), leader);
@@ -430,7 +438,7 @@ __device__ __forceinline__ void role_mma(const FwdParams& p, uint32_t sbase, uin
       vcnt = kv_cnt++;
     }
     if (!ok) break;
-    umma_commit(bar(L::kBarQEmpty), leader);  // all S MMAs of this work item issued: Q may be reloaded
+    umma_commit(bar(L::kBarQEmpty + 1), leader);  // last S1 of the item issued: Q1 may be reloaded
     const uint32_t vs = vcnt % kStages;
     if (!sy.wait(bar(L::kBarKVFull + vs), (vcnt / kStages) & 1u, kSiteMmaVFull)) { ok = false; break; }
     if (n0 == n1) {
