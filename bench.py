@@ -88,20 +88,54 @@ def load_traffic(workload: str):
 
 
 class ClockSampler:
-    """nvidia-smi -lms sampling of SM clock and throttle reasons for one GPU."""
+    """SM clock, power and clock-event (throttle) reasons of one GPU, sampled
+    every 50 ms during the run with the time of each sample.
 
+    Reads NVML directly (the source nvidia-smi prints from); nvidia-smi through
+    a pipe is block-buffered, so its lines cannot be matched to the timed
+    windows.  Falls back to nvidia-smi -lms when NVML is unavailable."""
+
+    # NVML clocks-event reason bits (nvmlClocksEventReason*)
+    REASONS = {0x4: "sw_power_cap", 0x8: "hw_slowdown", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown"}
     FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.proc = None
-        self.lines = []
+        vis = os.environ.get("CUDA_VISIBLE_DEVICES", "")
+        ids = [x.strip() for x in vis.split(",") if x.strip()]
+        self.gpu = int(ids[gpu_index]) if gpu_index < len(ids) and ids[gpu_index].isdigit() else gpu_index
+        self.samples = []  # (time, sm_mhz, max_mhz, watts, reason names)
+        self.stop_flag = False
         self.thread = None
-        self.marks = []
+        self.proc = None
 
     def start(self):
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.gpu)
+            max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            return self._start_smi()
+
+        def run():
+            while not self.stop_flag:
+                t = time.time()
+                try:
+                    mhz = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                    watts = pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0
+                    bits = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                except Exception:
+                    break
+                names = [n for b, n in self.REASONS.items() if bits & b]
+                self.samples.append((t, float(mhz), float(max_mhz), watts, names))
+                time.sleep(0.05)
+
+        self.thread = threading.Thread(target=run, daemon=True)
+        self.thread.start()
+
+    def _start_smi(self):
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "100"],
@@ -109,47 +143,41 @@ class ClockSampler:
         except OSError:
             self.proc = None
             return
-        self.thread = threading.Thread(target=self._read, daemon=True)
+
+        def read():
+            names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+            for line in self.proc.stdout:
+                parts = [x.strip() for x in line.split(",")]
+                try:
+                    self.samples.append((time.time(), float(parts[0]), float(parts[1]), float(parts[2]),
+                                         [n for n, v in zip(names, parts[4:8]) if v.lower().startswith("active")]))
+                except (ValueError, IndexError):
+                    continue
+
+        self.thread = threading.Thread(target=read, daemon=True)
         self.thread.start()
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append((time.time(), line.strip()))
-
-    def mark(self, name):
-        self.marks.append((name, time.time()))
-
     def stop(self):
+        self.stop_flag = True
         if self.proc is not None:
             self.proc.terminate()
             try:
                 self.proc.wait(timeout=5)
             except subprocess.TimeoutExpired:
                 self.proc.kill()
-            if self.thread is not None:
-                self.thread.join(timeout=2)
+        if self.thread is not None:
+            self.thread.join(timeout=2)
 
     def summary(self, windows):
-        """Samples that fall inside any of the (t0, t1) windows."""
-        sms, maxs, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for t, line in self.lines:
-            if not any(t0 <= t <= t1 for t0, t1 in windows):
-                continue
-            parts = [x.strip() for x in line.split(",")]
-            if len(parts) < 8:
-                continue
-            try:
-                sms.append(float(parts[0]))
-                maxs.append(float(parts[1]))
-            except ValueError:
-                continue
-            for name, val in zip(names, parts[4:8]):
-                if val.lower().startswith("active"):
-                    reasons.add(name)
-        if not sms:
+        """Median SM clock and power, max clock and every reason seen, over the
+        samples that fall inside any of the (t0, t1) windows."""
+        sel = [x for x in self.samples if any(t0 <= x[0] <= t1 for t0, t1 in windows)]
+        if not sel:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
-        return {"sm_mhz": statistics.median(sms), "sm_max_mhz": max(maxs), "reasons": sorted(reasons), "samples": len(sms)}
+        reasons = sorted({n for x in sel for n in x[4]})
+        return {"sm_mhz": statistics.median(x[1] for x in sel), "sm_max_mhz": max(x[2] for x in sel),
+                "power_w": round(statistics.median(x[3] for x in sel), 1), "reasons": reasons,
+                "samples": len(sel), "source": "nvml" if self.proc is None else "nvidia-smi"}
 
 
 def cpu_attention_rate(wl: Workload, budget_s: float, max_slices: int = 64):
