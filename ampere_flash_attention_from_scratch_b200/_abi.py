@@ -65,6 +65,7 @@ class AfaFwdArgs(ctypes.Structure):
         ("n_kv_heads", ctypes.c_int32),
         ("causal", ctypes.c_int32),
         ("lse", ctypes.c_void_p),
+        ("sched", ctypes.c_void_p),
     ]
 
 
@@ -97,7 +98,7 @@ def load() -> ctypes.CDLL:
 
 
 def make_args(q, k, v, o, status=None, scale=0.0, timeout_ns=0, test_flags=0, causal=False,
-              lse=None) -> AfaFwdArgs:
+              lse=None, sched=None) -> AfaFwdArgs:
     """AfaFwdArgs for torch tensors q, o [B, N, H, d] and k, v [B, N_kv, H_kv, d]
     (device memory); lse: optional fp32 [B, H, N] tensor."""
     dt = {"torch.float16": AFA_DTYPE_FP16, "torch.bfloat16": AFA_DTYPE_BF16}.get(str(q.dtype), -1)
@@ -114,6 +115,7 @@ def make_args(q, k, v, o, status=None, scale=0.0, timeout_ns=0, test_flags=0, ca
     a.seq_len_kv, a.n_kv_heads = int(k.shape[1]), int(k.shape[2])
     a.causal = 1 if causal else 0
     a.lse = lse.data_ptr() if lse is not None else None
+    a.sched = sched.data_ptr() if sched is not None else None
     return a
 
 

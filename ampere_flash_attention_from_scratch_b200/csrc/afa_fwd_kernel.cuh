@@ -75,6 +75,7 @@ struct FwdParams {
   int n_work;      // batch * n_heads * n_q_pairs
   int causal_off;  // seq_len_kv - seq_len: query row i sees keys j <= i + causal_off
   float* lse;      // optional [batch, n_heads, seq_len] fp32 log-sum-exp (natural log)
+  int* sched;      // optional scheduler words [2] (causal kernel): 0 at rest; null = static schedule
   float scale_log2;  // scale * log2(e)
   int* status;
   unsigned long long timeout_ns;
@@ -94,6 +95,8 @@ enum WaitSite : int {
   kSiteSoftmaxS = 8,
   kSiteSoftmaxO = 9,
   kSiteMmaDrain = 10,
+  kSiteLoadItem = 11,  // producer waiting for a free slot of the work-item ring
+  kSiteReadItem = 12,  // MMA / softmax warps waiting for the next claimed work item
 };
 
 // Compile-time layout of one kernel instance.
@@ -129,10 +132,17 @@ struct FwdLayout {
   static constexpr int kBarPReady = kBarSFull + 2;       // [2][kPChunks]
   static constexpr int kBarOFinal = kBarPReady + 2 * kPChunks;  // [2]
   static constexpr int kBarMmaDrain = kBarOFinal + 2;
-  static constexpr int kNumBars = kBarMmaDrain + 1;
+  // Dynamic schedule: ring of kItemSlots claimed work items (producer -> MMA
+  // warp and the 8 softmax warps).
+  static constexpr int kItemSlots = 4;
+  static constexpr int kBarItemFull = kBarMmaDrain + 1;           // [kItemSlots]
+  static constexpr int kBarItemEmpty = kBarItemFull + kItemSlots;  // [kItemSlots]
+  static constexpr uint32_t kItemReaders = 1 + 8;                 // MMA warp + softmax warps
+  static constexpr int kNumBars = kBarItemEmpty + kItemSlots;
   static constexpr uint32_t kOffTmemSlot = kOffBar + kNumBars * 8;
   static constexpr uint32_t kOffAbort = kOffTmemSlot + 4;
-  static constexpr uint32_t kSmemUsed = kOffAbort + 4;
+  static constexpr uint32_t kOffItems = kOffAbort + 4;            // int[kItemSlots]
+  static constexpr uint32_t kSmemUsed = kOffItems + 4 * kItemSlots;
   static constexpr uint32_t kSmemBytes = kSmemUsed + 1024;  // slack for 1024-byte alignment
   static constexpr int kThreads = 384;
   static constexpr int kSoftmaxThreads = 128;
@@ -241,6 +251,69 @@ __device__ __forceinline__ void decode_work(const FwdParams& p, int w, int& qp, 
   b = bh / p.n_heads;
 }
 
+// The work items a CTA processes, in order.  Static: blockIdx.x, then every
+// gridDim.x-th item.  Dynamic (the causal kernel given scheduler words): the
+// producer claims the next item with atomicAdd on sched[0] and publishes it in
+// a ring of kItemSlots shared-memory slots, which the MMA warp and the softmax
+// warps read in the same order; items of very different length then even out
+// across SMs while consecutive items (the same head's K/V, in L2) still run at
+// the same time.  After its last claim each CTA counts itself on sched[1]; the
+// last one returns both words to 0 for the next launch.
+template <int kSlots>
+struct WorkQueue {
+  int* sched;             // null: static schedule
+  volatile int* slots;    // [kSlots]
+  uint32_t full0, empty0; // item_full / item_empty barriers
+  int n_work;
+  static constexpr int kDone = -1;   // no more items
+  static constexpr int kAbort = -2;  // a bounded wait ran out
+
+  __device__ __forceinline__ bool dynamic() const { return sched != nullptr; }
+
+  // Producer (whole warp, converged): item number `it` of this CTA.
+  __device__ __forceinline__ int claim(uint32_t it, const CtaSync& sy, int site) const {
+    if (!dynamic()) {
+      const int w = static_cast<int>(blockIdx.x + it * gridDim.x);
+      return w < n_work ? w : kDone;
+    }
+    const uint32_t slot = it % kSlots, ph = (it / kSlots) & 1u;
+    if (!sy.wait(empty0 + 8u * slot, ph ^ 1u, site)) return kAbort;
+    int w = 0;
+    if ((threadIdx.x & 31u) == 0u) {
+      w = atomicAdd(sched, 1);
+      if (w >= n_work) w = kDone;
+      slots[slot] = w;
+      mbar_arrive(full0 + 8u * slot);  // release: the slot write is visible to the readers
+    }
+    return __shfl_sync(0xffffffffu, w, 0);
+  }
+
+  // Readers (whole warp, converged): the same sequence.
+  __device__ __forceinline__ int next(uint32_t it, const CtaSync& sy, int site) const {
+    if (!dynamic()) {
+      const int w = static_cast<int>(blockIdx.x + it * gridDim.x);
+      return w < n_work ? w : kDone;
+    }
+    const uint32_t slot = it % kSlots, ph = (it / kSlots) & 1u;
+    if (!sy.wait(full0 + 8u * slot, ph, site)) return kAbort;
+    const int w = slots[slot];
+    __syncwarp();
+    if ((threadIdx.x & 31u) == 0u) mbar_arrive(empty0 + 8u * slot);
+    return w;
+  }
+
+  // Producer, after its last claim (or an abort): count this CTA; the last
+  // CTA resets the words.  Every claim of every CTA precedes its count.
+  __device__ __forceinline__ void finish() const {
+    if (!dynamic() || (threadIdx.x & 31u) != 0u) return;
+    __threadfence();
+    if (atomicAdd(sched + 1, 1) == static_cast<int>(gridDim.x) - 1) {
+      atomicExch(sched, 0);
+      atomicExch(sched + 1, 0);
+    }
+  }
+};
+
 // K/V tiles that Q tile t (0 or 1) of q-pair qp must visit: all of them, or
 // under the causal mask those up to the last key its last query row sees
 // (at least one, so a tile whose rows see no key still finishes with O = 0).
@@ -259,7 +332,7 @@ __device__ __forceinline__ int kv_tiles(const FwdParams& p, int qp, int t) {
 // ---------------------------------------------------------------------------
 template <int kD, bool kBF16, int kStages, bool kCausal>
 __device__ __forceinline__ void role_load(const FwdParams& p, uint32_t sbase, uint32_t bar0,
-                                          const CtaSync& sy) {
+                                          const CtaSync& sy, const WorkQueue<4>& wq) {
   using L = FwdLayout<kD, kBF16, kStages>;
   auto bar = [&](int i) { return bar0 + 8u * static_cast<uint32_t>(i); };
   const uint64_t pol_kv = l2_policy_evict_last();
@@ -269,8 +342,14 @@ __device__ __forceinline__ void role_load(const FwdParams& p, uint32_t sbase, ui
   uint32_t kv_cnt = 0, q_cnt[2] = {0u, 0u};
   uint32_t it = 0;
   bool ok = true;
-  if (p.test_flags & 1u) return;  // nothing is loaded: the consumers' bounded waits run out
-  for (int w = blockIdx.x; w < p.n_work && ok; w += gridDim.x, ++it) {
+  if (p.test_flags & 1u) {  // nothing is loaded: the consumers' bounded waits run out
+    wq.finish();
+    return;
+  }
+  for (;; ++it) {
+    const int w = wq.claim(it, sy, kSiteLoadItem);
+    if (w == wq.kAbort) { ok = false; break; }
+    if (w < 0) break;
     int qp, h, b;
     decode_work<kCausal>(p, w, qp, h, b);
     const int h_kv = p.kv_group == 1 ? h : h / p.kv_group;
@@ -310,7 +389,9 @@ __device__ __forceinline__ void role_load(const FwdParams& p, uint32_t sbase, ui
         ++kv_cnt;
       }
     }
+    if (!ok) break;
   }
+  wq.finish();
   if (ok) return;
   // Aborted: before the CTA may exit, wait (bounded, not cut short by the
   // abort flag) until the loads still in flight have landed -- the last
@@ -363,7 +444,7 @@ __device__ __forceinline__ void issue_pv_chunk(uint32_t d_tmem, uint32_t p_tmem,
 
 template <int kD, bool kBF16, int kStages, bool kCausal>
 __device__ __forceinline__ void role_mma(const FwdParams& p, uint32_t sbase, uint32_t bar0,
-                                         uint32_t tmem, const CtaSync& sy) {
+                                         uint32_t tmem, const CtaSync& sy, const WorkQueue<4>& wq) {
   using L = FwdLayout<kD, kBF16, kStages>;
   auto bar = [&](int i) { return bar0 + 8u * static_cast<uint32_t>(i); };
   auto slot_addr = [&](uint32_t s) { return sbase + L::kOffKV + s * L::kTileBytes; };
@@ -387,7 +468,9 @@ __device__ __forceinline__ void role_mma(const FwdParams& p, uint32_t sbase, uin
     return true;
   };
   bool ok = (p.test_flags & 2u) == 0u;  // bit 1: issue nothing; the other roles' waits run out
-  for (int w = blockIdx.x; w < p.n_work && ok; w += gridDim.x, ++it) {
+  for (; ok; ++it) {
+    const int w = wq.next(it, sy, kSiteReadItem);
+    if (w < 0) break;  // done, or aborted
     // Q tile 0 visits n0 K/V tiles, Q tile 1 n1 >= n0 (equal without a causal
     // mask; the work item is only decoded when they can differ, since this
     // warp's integer divisions delay the item's first MMA).
@@ -460,7 +543,7 @@ __device__ __forceinline__ void role_mma(const FwdParams& p, uint32_t sbase, uin
 // ---------------------------------------------------------------------------
 template <int kD, bool kBF16, int kStages, bool kCausal>
 __device__ __forceinline__ void role_softmax(const FwdParams& p, int wg, uint32_t bar0,
-                                             uint32_t tmem, const CtaSync& sy) {
+                                             uint32_t tmem, const CtaSync& sy, const WorkQueue<4>& wq) {
   using L = FwdLayout<kD, kBF16, kStages>;
   using T = typename std::conditional<kBF16, __nv_bfloat16, __half>::type;
   auto bar = [&](int i) { return bar0 + 8u * static_cast<uint32_t>(i); };
@@ -476,7 +559,9 @@ __device__ __forceinline__ void role_softmax(const FwdParams& p, int wg, uint32_
   const uint32_t bar_o = bar(L::kBarOFinal + wg);
   uint32_t sph = 0, oph = 0;
 
-  for (int w = blockIdx.x; w < p.n_work; w += gridDim.x) {
+  for (uint32_t it = 0;; ++it) {
+    const int w = wq.next(it, sy, kSiteReadItem);
+    if (w < 0) return;  // done, or aborted
     int qp, h, b;
     decode_work<kCausal>(p, w, qp, h, b);
     const int q_row = qp * 256 + wg * 128 + row;
@@ -633,7 +718,9 @@ __global__ void __launch_bounds__(384, 1) afa_fwd_sm100_kernel(const __grid_cons
   if (warp == 0 && lane == 0) {
     for (int i = 0; i < L::kNumBars; ++i) {
       // p_ready: one elected arrival per softmax warp; all others: one arrival.
-      const uint32_t count = (i >= L::kBarPReady && i < L::kBarPReady + 2 * L::kPChunks) ? 4u : 1u;
+      uint32_t count = 1u;
+      if (i >= L::kBarPReady && i < L::kBarPReady + 2 * L::kPChunks) count = 4u;
+      if (i >= L::kBarItemEmpty && i < L::kBarItemEmpty + L::kItemSlots) count = L::kItemReaders;
       mbar_init(bar0 + 8u * i, count);
     }
     *abort_flag = 0;
@@ -651,17 +738,22 @@ __global__ void __launch_bounds__(384, 1) afa_fwd_sm100_kernel(const __grid_cons
   tc_fence_after_sync();
   const uint32_t tmem = *reinterpret_cast<volatile uint32_t*>(tmem_slot);
   const CtaSync sy{abort_flag, p.status, p.timeout_ns};
+  // Dynamic schedule only for the causal kernel (items of unequal length) and
+  // only with caller-provided scheduler words.
+  const WorkQueue<L::kItemSlots> wq{kCausal ? p.sched : nullptr,
+                                    reinterpret_cast<volatile int*>(smem + L::kOffItems),
+                                    bar0 + 8u * L::kBarItemFull, bar0 + 8u * L::kBarItemEmpty, p.n_work};
 
   if (warp < 4) {
     setmaxnreg_dec<L::kProducerRegs>();
     if (warp == 0) {
-      role_load<kD, kBF16, kStages, kCausal>(p, sbase, bar0, sy);
+      role_load<kD, kBF16, kStages, kCausal>(p, sbase, bar0, sy, wq);
     } else if (warp == 1) {
-      role_mma<kD, kBF16, kStages, kCausal>(p, sbase, bar0, tmem, sy);
+      role_mma<kD, kBF16, kStages, kCausal>(p, sbase, bar0, tmem, sy, wq);
     }
   } else {
     setmaxnreg_inc<L::kSoftmaxRegs>();
-    role_softmax<kD, kBF16, kStages, kCausal>(p, (warp - 4) >> 2, bar0, tmem, sy);
+    role_softmax<kD, kBF16, kStages, kCausal>(p, (warp - 4) >> 2, bar0, tmem, sy, wq);
   }
 
   tc_fence_before_sync();

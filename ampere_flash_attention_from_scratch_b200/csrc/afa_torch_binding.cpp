@@ -29,6 +29,7 @@
 #include <cuda_runtime.h>
 #include <torch/extension.h>
 
+#include <map>
 #include <mutex>
 #include <optional>
 #include <string>
@@ -81,10 +82,27 @@ at::Tensor& status_word(const at::Device& dev) {
   return g_status[i];
 }
 
+// Scheduler words of the causal kernel (AfaFwdArgs.sched), one pair per
+// (device, stream) so launches that may overlap never share them; zero at rest.
+std::map<std::pair<int, cudaStream_t>, at::Tensor> g_sched;
+
+int32_t* sched_words(const at::Device& dev, cudaStream_t stream) {
+  std::lock_guard<std::mutex> lock(g_status_mu);
+  at::Tensor& t = g_sched[{static_cast<int>(dev.index()), stream}];
+  if (!t.defined()) t = at::zeros({2}, at::TensorOptions().dtype(at::kInt).device(dev));
+  return t.data_ptr<int32_t>();
+}
+
 int32_t read_and_clear_status(const at::Device& dev) {
   at::Tensor& s = status_word(dev);
   const int32_t v = s.item<int32_t>();
-  if (v != 0) s.zero_();
+  if (v != 0) {
+    s.zero_();
+    // A kernel that stopped early may not have returned its scheduler words to zero.
+    std::lock_guard<std::mutex> lock(g_status_mu);
+    for (auto& kv : g_sched)
+      if (kv.first.first == static_cast<int>(dev.index())) kv.second.zero_();
+  }
   return v;
 }
 
@@ -179,6 +197,7 @@ float launch(const at::Tensor& TQ, const at::Tensor& TK, const at::Tensor& TV, c
   args.lse = lse;
 
   cudaStream_t stream = at::cuda::getCurrentCUDAStream().stream();
+  args.sched = causal ? sched_words(TQ.device(), stream) : nullptr;
   float runtime = 0.f;
   cudaEvent_t start = nullptr, stop = nullptr;
   if (benchmark) {

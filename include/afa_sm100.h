@@ -34,7 +34,7 @@ extern "C" {
 #define AFA_ERR_INVALID_ARGUMENT 1   /* null pointer, non-positive size, n_kv_heads not dividing n_heads, causal not 0/1 */
 #define AFA_ERR_UNSUPPORTED_DTYPE 2  /* dtype not fp16/bf16 */
 #define AFA_ERR_NO_KERNEL 3          /* no compiled kernel for (dtype, head_dim) */
-#define AFA_ERR_MISALIGNED 4         /* base address / stride not 16-byte aligned */
+#define AFA_ERR_MISALIGNED 4         /* base address / stride not 16-byte aligned (lse: 4, sched: 8) */
 #define AFA_ERR_NO_DEVICE 5          /* no current CUDA device */
 #define AFA_ERR_ARCH 6               /* device is not compute capability 10.0 */
 #define AFA_ERR_TENSOR_MAP 7         /* cuTensorMapEncodeTiled rejected a tensor */
@@ -76,6 +76,12 @@ typedef struct AfaFwdArgs {
   float* lse;          /* optional device fp32 [batch, n_heads, seq_len], contiguous:
                           ln(sum_j exp(scale * q_i . k_j)) over the keys row i sees,
                           -inf for a row that sees none.  NULL: not written */
+  int32_t* sched;      /* optional device int32[2], 8-byte aligned, zero before first use:
+                          scheduler words of the causal kernel, which then hands out work
+                          items dynamically (atomic counter) instead of round-robin; the
+                          kernel returns them to zero when it ends.  One launch at a time
+                          per pair of words: launches that may overlap (other streams) need
+                          their own.  Ignored without the causal mask.  NULL: static schedule */
 } AfaFwdArgs;
 
 /* test_flags bit: the kernel's TMA producer issues no loads, so the first

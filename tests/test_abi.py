@@ -88,6 +88,7 @@ def valid_args(**over):
         ({"seq_len_kv": -5}, _abi.AFA_ERR_INVALID_ARGUMENT),
         ({"causal": 2}, _abi.AFA_ERR_INVALID_ARGUMENT),
         ({"lse": 0x100002}, _abi.AFA_ERR_MISALIGNED),
+        ({"sched": 0x100004}, _abi.AFA_ERR_MISALIGNED),
         ({"seq_len_kv": (1 << 31) - 100}, _abi.AFA_ERR_TOO_LARGE),
     ],
 )
