@@ -180,9 +180,10 @@ class ClockSampler:
                 "samples": len(sel), "source": "nvml" if self.proc is None else "nvidia-smi"}
 
 
-def cpu_attention_rate(wl: Workload, budget_s: float, max_slices: int = 64):
+def cpu_attention_rate(wl: Workload, budget_s: float, max_slices: int = 64, causal: bool = False):
     """Naive torch fp32 attention on the host cores over (b, h) slices until the
-    time budget is spent; returns (TFLOP/s, slices, seconds, threads)."""
+    time budget is spent; returns (TFLOP/s, slices, seconds, threads).  With
+    the causal mask half the FLOPs are counted, as for the GPU number."""
     from oracle.attention_oracle import attention_fp32  # the CPU baseline only
 
     threads = os.cpu_count() or 1
@@ -192,12 +193,12 @@ def cpu_attention_rate(wl: Workload, budget_s: float, max_slices: int = 64):
     q = (torch.randn(1, N, 1, d, generator=g) * wl.sigma_qk).to(wl.dtype)
     k = (torch.randn(1, N, 1, d, generator=g) * wl.sigma_qk).to(wl.dtype)
     v = torch.randn(1, N, 1, d, generator=g).to(wl.dtype)
-    attention_fp32(q, k, v)  # warm-up (allocator, thread pool)
-    flops_slice = 4 * N * N * d
+    attention_fp32(q, k, v, causal=causal)  # warm-up (allocator, thread pool)
+    flops_slice = 4 * N * N * d // (2 if causal else 1)
     t0 = time.perf_counter()
     n = 0
     while n < max_slices:
-        attention_fp32(q, k, v)
+        attention_fp32(q, k, v, causal=causal)
         n += 1
         if time.perf_counter() - t0 >= budget_s:
             break
@@ -253,7 +254,7 @@ def run_reference(args, wl: Workload):
     print(json.dumps(line), flush=True)
 
 
-def workload_config(wl: Workload, n_gpus: int):
+def workload_config(wl: Workload, n_gpus: int, causal: bool = False):
     return {
         "workload": wl.name,
         "shape_BNHd": list(wl.shape),
@@ -261,7 +262,7 @@ def workload_config(wl: Workload, n_gpus: int):
         "seq_len": wl.seq_len,
         "n_heads": wl.n_heads,
         "head_dim": wl.d_head,
-        "causal": False,
+        "causal": causal,
         "sigma_qk": wl.sigma_qk,
         "parallelism": f"batch split over {n_gpus} GPU(s), no collective on the data path",
         "l2": f"inputs {3 * wl.hbm_bytes // 4 / 1e9:.2f} GB > 126 MB L2, no flush between steps",
@@ -293,8 +294,16 @@ def run_ours(args, wl: Workload):
     o = torch.empty_like(q)
     cfg = AFAForwardKernelConfig(dtype=DType.FP16 if wl.dtype == torch.float16 else DType.BF16, d_head=wl.d_head)
     stream = torch.cuda.current_stream()
-    flops_rank = wl.flops // world
+    # Causal (bottom-right mask, forward_ext with the dynamic schedule): half the
+    # 4*B*H*N^2*d FLOPs are counted, as for FlashAttention's causal numbers.
+    causal = bool(args.causal)
+    flops_rank = wl.flops // world // (2 if causal else 1)
     total_flops = flops_rank * world
+
+    def fwd(q_, k_, v_, o_):
+        if causal:
+            return fa.forward_ext(q_, k_, v_, o_, True)[0]
+        return fa.forward(cfg, q_, k_, v_, o_, False)[0]
 
     def barrier():
         torch.cuda.synchronize()
@@ -311,7 +320,7 @@ def run_ours(args, wl: Workload):
 
     # --- device-resident timing ------------------------------------------
     for _ in range(args.warmup):
-        fa.forward(cfg, q, k, v, o, False)
+        fwd(q, k, v, o)
     barrier()
     fa.check_status(local_rank)
     ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
@@ -319,7 +328,7 @@ def run_ours(args, wl: Workload):
     w0 = time.time()
     for s, e in ev:
         s.record(stream)
-        fa.forward(cfg, q, k, v, o, False)
+        fwd(q, k, v, o)
         e.record(stream)
     barrier()
     w1 = time.time()
@@ -336,7 +345,7 @@ def run_ours(args, wl: Workload):
     e2e_steps = max(1, min(args.steps, args.e2e_steps))
     for _ in range(min(2, args.warmup)):
         qd, kd, vd = (t.to(dev, non_blocking=True) for t in (qh, kh, vh))
-        od, _ = fa.forward(cfg, qd, kd, vd, None, False)
+        od = fwd(qd, kd, vd, None)
         oh.copy_(od, non_blocking=True)
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -345,7 +354,7 @@ def run_ours(args, wl: Workload):
     e0.record(stream)
     for _ in range(e2e_steps):
         qd, kd, vd = (t.to(dev, non_blocking=True) for t in (qh, kh, vh))
-        od, _ = fa.forward(cfg, qd, kd, vd, None, False)
+        od = fwd(qd, kd, vd, None)
         oh.copy_(od, non_blocking=True)
     e1.record(stream)
     barrier()
@@ -364,7 +373,7 @@ def run_ours(args, wl: Workload):
     # --- CPU baseline (rank 0, N = 1 only) -------------------------------------
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        rate, n, secs, threads = cpu_attention_rate(wl, args.cpu_budget)
+        rate, n, secs, threads = cpu_attention_rate(wl, args.cpu_budget, causal=causal)
         cpu = {
             "value": rate,
             "unit": "TFLOP/s",
@@ -377,7 +386,7 @@ def run_ours(args, wl: Workload):
     if rank == 0:
         peaks, peak_src = load_peaks()
         peak = float(peaks.get("bf16_tflops", FALLBACK_PEAK["bf16_tflops"]))
-        traffic = load_traffic(wl.name)
+        traffic = load_traffic(wl.name + ("-causal" if causal else ""))
         if traffic is not None and world > 1:
             traffic = traffic // world
         line = {
@@ -393,7 +402,7 @@ def run_ours(args, wl: Workload):
             "vs_baseline": None,
             "dtype": wl.dtype_name(),
             "data": "synthetic",
-            "config": workload_config(wl, world),
+            "config": workload_config(wl, world, causal),
             "frac_of_nominal_dense_peak": value / (NOMINAL_DENSE_TFLOPS * world),
             "roofline": {
                 "bound": "tensor",
@@ -429,10 +438,15 @@ def main():
     ap.add_argument("--e2e-steps", type=int, default=10)
     ap.add_argument("--cpu-budget", type=float, default=10.0, help="seconds of CPU-baseline work")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--causal", action="store_true",
+                    help="causal mask (forward_ext, dynamic work schedule); half the FLOPs are counted")
     args = ap.parse_args()
     args.warmup = max(3, args.warmup)  # at least 3 untimed warm-up steps (reported as used)
     wl = WORKLOADS[args.config]
     if args.impl == "reference":
+        if args.causal:
+            print(json.dumps({"impl": "reference", "unavailable": "the reference has no causal mask"}), flush=True)
+            return
         run_reference(args, wl)
     else:
         run_ours(args, wl)
