@@ -27,12 +27,14 @@ AFA_ERR_LAUNCH = 8
 AFA_ERR_DEVICE_TIMEOUT = 9
 AFA_ERR_TOO_LARGE = 10
 AFA_DEV_TIMEOUT_BASE = 0x100
+AFA_NOALLOC_SCRATCH_BYTES = 256
 AFA_TEST_PRODUCER_IDLE = 1
 AFA_TEST_MMA_IDLE = 2
 
 # Every extern "C" symbol declared in include/afa_sm100.h.
 EXPORTED_SYMBOLS = (
     "afa_fwd_sm100",
+    "afa_fwd_sm100_noalloc",
     "afa_strerror",
     "afa_status_string",
     "afa_fwd_sm100_supported",
@@ -81,6 +83,8 @@ def load() -> ctypes.CDLL:
         lib = ctypes.CDLL(str(LIB_PATH))
         lib.afa_fwd_sm100.argtypes = [ctypes.POINTER(AfaFwdArgs), ctypes.c_void_p]
         lib.afa_fwd_sm100.restype = ctypes.c_int
+        lib.afa_fwd_sm100_noalloc.argtypes = [ctypes.POINTER(AfaFwdArgs), ctypes.c_void_p]
+        lib.afa_fwd_sm100_noalloc.restype = ctypes.c_int
         lib.afa_strerror.argtypes = [ctypes.c_int]
         lib.afa_strerror.restype = ctypes.c_char_p
         lib.afa_status_string.argtypes = [ctypes.c_int32]

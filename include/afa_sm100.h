@@ -107,6 +107,25 @@ typedef struct AfaFwdArgs {
  */
 int afa_fwd_sm100(const AfaFwdArgs* args, void* stream);
 
+/*
+ * afa_fwd_sm100 without caller-provided scratch memory.  The only scratch any
+ * call needs is the causal kernel's two scheduler words (AfaFwdArgs.sched); this
+ * entry point takes them from a static, 256-byte-aligned __device__ array inside
+ * the library (AFA_NOALLOC_SCRATCH_BYTES per device, located with
+ * cudaGetSymbolAddress on the current device) instead, so args->sched must be
+ * NULL (else AFA_ERR_INVALID_ARGUMENT), and a call needing more scratch than the
+ * array holds is rejected with AFA_ERR_TOO_LARGE.  Before a causal launch it
+ * clears exactly the words the kernel requires to start at zero
+ * (cudaMemsetAsync on `stream`); it never allocates or frees memory.
+ * Races: every call on a device shares that array, so calls that may run at the
+ * same time on one device (different streams or host threads without ordering
+ * between them) must not both be causal; order them on one stream, or give each
+ * its own words through afa_fwd_sm100.  Otherwise identical to afa_fwd_sm100,
+ * with bit-identical results.
+ */
+#define AFA_NOALLOC_SCRATCH_BYTES 256
+int afa_fwd_sm100_noalloc(const AfaFwdArgs* args, void* stream);
+
 /* Human-readable text for an AFA_* return code (static storage). */
 const char* afa_strerror(int code);
 

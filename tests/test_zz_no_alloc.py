@@ -1,0 +1,71 @@
+"""afa_fwd_sm100_noalloc: the entry point whose scratch memory (the causal
+kernel's scheduler words) comes from a static __device__ array in the library
+instead of the caller.  Checked against the existing entry point
+(afa_fwd_sm100 with caller-owned words) on two consecutive calls: results must
+be bit-identical, and the static words are reused from one call to the next."""
+
+import ctypes
+
+import pytest
+import torch
+
+from ampere_flash_attention_from_scratch_b200 import _abi
+
+
+def _valid_args(**over):
+    a = _abi.AfaFwdArgs()
+    a.q = a.k = a.v = a.o = 0x100000
+    for name in ("q_strides", "k_strides", "v_strides", "o_strides"):
+        getattr(a, name)[:] = [1024 * 4 * 128, 4 * 128, 128]
+    a.batch, a.seq_len, a.n_heads, a.head_dim = 2, 1024, 4, 128
+    a.dtype = _abi.AFA_DTYPE_FP16
+    for k, v in over.items():
+        setattr(a, k, v)
+    return a
+
+
+def test_exported_and_rejects_caller_words_without_gpu():
+    lib = _abi.load()
+    assert hasattr(lib, "afa_fwd_sm100_noalloc")
+    # Caller-provided scheduler words are refused (the static array is used instead),
+    # before any CUDA call is made.
+    a = _valid_args(causal=1, sched=0x200000)
+    assert lib.afa_fwd_sm100_noalloc(ctypes.byref(a), None) == _abi.AFA_ERR_INVALID_ARGUMENT
+    # Argument errors are the same as the existing entry point's.
+    for over, code in (({"dtype": 7}, _abi.AFA_ERR_UNSUPPORTED_DTYPE), ({"head_dim": 96}, _abi.AFA_ERR_NO_KERNEL),
+                       ({"q": None}, _abi.AFA_ERR_INVALID_ARGUMENT)):
+        a = _valid_args(**over)
+        assert lib.afa_fwd_sm100_noalloc(ctypes.byref(a), None) == code == lib.afa_fwd_sm100(ctypes.byref(a), None)
+    assert lib.afa_fwd_sm100_noalloc(None, None) == _abi.AFA_ERR_INVALID_ARGUMENT
+
+
+def _inputs(B, N, NK, H, HK, d, seed):
+    g = torch.Generator().manual_seed(seed)
+    q = torch.randn(B, N, H, d, generator=g).half().cuda()
+    k = torch.randn(B, NK, HK, d, generator=g).half().cuda()
+    v = torch.randn(B, NK, HK, d, generator=g).half().cuda()
+    return q, k, v
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("causal", [True, False])
+def test_matches_existing_entry_point_on_two_calls(causal):
+    lib = _abi.load()
+    stream = torch.cuda.current_stream().cuda_stream
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    words = torch.zeros(2, dtype=torch.int32, device="cuda")
+    for call, shape in enumerate([(2, 2000, 2000, 8, 2, 128), (1, 777, 1500, 4, 4, 64)]):
+        q, k, v = _inputs(*shape, seed=call)
+        B, N, H = shape[0], shape[1], shape[3]
+        outs = []
+        for entry, sched in ((lib.afa_fwd_sm100, words if causal else None), (lib.afa_fwd_sm100_noalloc, None)):
+            o = torch.empty_like(q)
+            lse = torch.empty(B, H, N, device="cuda")
+            a = _abi.make_args(q, k, v, o, status=status, causal=causal, lse=lse, sched=sched)
+            assert entry(ctypes.byref(a), stream) == _abi.AFA_OK
+            torch.cuda.synchronize()
+            assert int(status.item()) == 0, lib.afa_status_string(int(status.item()))
+            outs.append((o, lse))
+        assert torch.equal(outs[0][0], outs[1][0]), f"call {call}: O differs"
+        assert torch.equal(outs[0][1], outs[1][1]), f"call {call}: lse differs"
+        assert words.tolist() == [0, 0]
