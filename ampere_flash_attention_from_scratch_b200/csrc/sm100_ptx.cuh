@@ -96,7 +96,7 @@ __device__ __forceinline__ bool mbar_try_wait_suspend(uint32_t bar, uint32_t par
 }
 
 // ---------------------------------------------------------------------------
-// TMA (bulk tensor copies).  Never used with .multicast::cluster.
+// TMA (bulk tensor copies).  Every load lands in one CTA only (no multicast).
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void tma_prefetch_desc(const CUtensorMap* map) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
