@@ -35,6 +35,6 @@ def _load_extension():
 
 
 def __getattr__(name):
-    if name in ("forward", "forward_ext", "check_status", "kernel_keys"):
+    if name in ("forward", "forward_ext", "forward_host", "check_status", "kernel_keys"):
         return getattr(_load_extension(), name)
     raise AttributeError(name)

@@ -25,10 +25,12 @@
 // with K/V of their own length and head count (GQA), the causal mask and the
 // fp32 log-sum-exp [batch, heads, seq] (None unless return_lse).
 #include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAStream.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <cuda_runtime.h>
 #include <torch/extension.h>
 
+#include <algorithm>
 #include <map>
 #include <mutex>
 #include <optional>
@@ -284,6 +286,124 @@ std::tuple<at::Tensor, std::optional<at::Tensor>> forward_ext(
   return std::make_tuple(TO, lse);
 }
 
+// Host-resident inputs and output: q [B, N, H, d], k, v [B, N_kv, H_kv, d] and O
+// in host memory (contiguous; page-locked for the copies to overlap).  The batch
+// is split into `chunks` slices that flow through two sets of device buffers on
+// three streams: while the kernel runs on slice c (the current stream), slice
+// c+1 is copied in and slice c-1 copied out, so the transfers over the host link
+// overlap each other and the compute.  Stream-ordered: returns after queuing;
+// the current stream is ordered after the last copy out.  Returns O (host).
+at::Tensor forward_host(const at::Tensor& HQ, const at::Tensor& HK, const at::Tensor& HV,
+                        std::optional<at::Tensor> out_, bool causal, int64_t chunks) {
+  for (const at::Tensor* t : {&HQ, &HK, &HV}) {
+    TORCH_CHECK(t->device().is_cpu(), "forward_host takes host (CPU) tensors");
+    TORCH_CHECK(t->dim() == 4 && t->is_contiguous(), "inputs must be contiguous [batch, seq, heads, head_dim]");
+  }
+  const int dt = dtype_code(HQ);
+  TORCH_CHECK(dt > 0, "Only fp16 and bf16 are supported");
+  TORCH_CHECK(HK.dtype() == HQ.dtype() && HV.dtype() == HQ.dtype(), "Input tensors must have the same data type");
+  TORCH_CHECK(HK.sizes() == HV.sizes(), "key and value tensors must have the same shape");
+  TORCH_CHECK(HK.size(0) == HQ.size(0) && HK.size(3) == HQ.size(3), "query and key batch / head_dim differ");
+  TORCH_CHECK(HQ.size(0) > 0 && HQ.size(1) > 0 && HQ.size(2) > 0 && HK.size(1) > 0 && HK.size(2) > 0,
+              "batch, seq_len and n_heads must be positive");
+  TORCH_CHECK(HQ.size(2) % HK.size(2) == 0, "the number of query heads (", HQ.size(2),
+              ") must be a multiple of the number of key/value heads (", HK.size(2), ")");
+  TORCH_CHECK(afa_fwd_sm100_supported(dt, static_cast<int32_t>(HQ.size(3))) == 1,
+              "no sm_100a kernel for head_dim ", HQ.size(3), " (64 and 128 are compiled)");
+  at::Tensor HO;
+  if (out_.has_value() && out_->defined()) {
+    HO = out_.value();
+    TORCH_CHECK(HO.device().is_cpu() && HO.is_contiguous() && HO.sizes() == HQ.sizes() && HO.dtype() == HQ.dtype(),
+                "o must be a contiguous host tensor shaped and typed like q");
+  } else {
+    HO = at::empty(HQ.sizes(), HQ.options().pinned_memory(true));
+  }
+  const int dev = c10::cuda::current_device();
+  int major = 0, minor = 0;
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+  TORCH_CHECK(major == 10 && minor == 0,
+              "Flash Attention (sm_100a build) requires SM_100 (current: SM_", major, ".", minor, ")");
+
+  const int64_t B = HQ.size(0);
+  const int64_t n_chunks = std::max<int64_t>(1, std::min<int64_t>(chunks > 0 ? chunks : 8, B));
+  const int64_t per = (B + n_chunks - 1) / n_chunks;  // batches per slice
+  const auto dopt = HQ.options().device(at::kCUDA, dev).pinned_memory(false);
+  auto slice_shape = [&](const at::Tensor& t) {
+    std::vector<int64_t> sz(t.sizes().begin(), t.sizes().end());
+    sz[0] = per;
+    return sz;
+  };
+  at::Tensor dq[2], dk[2], dv[2], dout[2];
+  for (int i = 0; i < 2; ++i) {
+    dq[i] = at::empty(slice_shape(HQ), dopt);
+    dk[i] = at::empty(slice_shape(HK), dopt);
+    dv[i] = at::empty(slice_shape(HV), dopt);
+    dout[i] = at::empty(slice_shape(HQ), dopt);
+  }
+  c10::cuda::CUDAStream comp = at::cuda::getCurrentCUDAStream();
+  c10::cuda::CUDAStream h2d = c10::cuda::getStreamFromPool(false, static_cast<c10::DeviceIndex>(dev));
+  c10::cuda::CUDAStream d2h = c10::cuda::getStreamFromPool(false, static_cast<c10::DeviceIndex>(dev));
+  cudaEvent_t start, h2d_done[2], comp_done[2], d2h_done[2];
+  auto mk = [](cudaEvent_t* e) {
+    TORCH_CHECK(cudaEventCreateWithFlags(e, cudaEventDisableTiming) == cudaSuccess, "cudaEventCreate failed");
+  };
+  mk(&start);
+  for (int i = 0; i < 2; ++i) {
+    mk(&h2d_done[i]);
+    mk(&comp_done[i]);
+    mk(&d2h_done[i]);
+  }
+  // The buffers were taken from the current stream's pool: earlier work on it
+  // completes before the copy stream writes them.
+  cudaEventRecord(start, comp.stream());
+  cudaStreamWaitEvent(h2d.stream(), start, 0);
+  const size_t esz = HQ.element_size();
+  auto row_bytes = [&](const at::Tensor& t) { return static_cast<size_t>(t.numel() / t.size(0)) * esz; };
+  for (int64_t c = 0; c < n_chunks; ++c) {
+    const int64_t b0 = c * per;
+    if (b0 >= B) break;
+    const int64_t nb = std::min(per, B - b0);
+    const int s = static_cast<int>(c & 1);
+    // in: slice c -> buffer set s, after the kernel of slice c-2 has read it
+    if (c >= 2) cudaStreamWaitEvent(h2d.stream(), comp_done[s], 0);
+    const at::Tensor* hs[3] = {&HQ, &HK, &HV};
+    at::Tensor* ds[3] = {&dq[s], &dk[s], &dv[s]};
+    for (int t = 0; t < 3; ++t) {
+      const size_t rb = row_bytes(*hs[t]);
+      TORCH_CHECK(cudaMemcpyAsync(ds[t]->data_ptr(), static_cast<const char*>(hs[t]->data_ptr()) + b0 * rb, nb * rb,
+                                  cudaMemcpyHostToDevice, h2d.stream()) == cudaSuccess,
+                  "host-to-device copy failed");
+    }
+    cudaEventRecord(h2d_done[s], h2d.stream());
+    // compute: after the slice is in and buffer set s's previous O has been copied out
+    cudaStreamWaitEvent(comp.stream(), h2d_done[s], 0);
+    if (c >= 2) cudaStreamWaitEvent(comp.stream(), d2h_done[s], 0);
+    launch(dq[s].narrow(0, 0, nb), dk[s].narrow(0, 0, nb), dv[s].narrow(0, 0, nb), dout[s].narrow(0, 0, nb), dt, 0.f,
+           causal, nullptr, false);
+    cudaEventRecord(comp_done[s], comp.stream());
+    // out: O of slice c
+    cudaStreamWaitEvent(d2h.stream(), comp_done[s], 0);
+    const size_t rb = row_bytes(HQ);
+    TORCH_CHECK(cudaMemcpyAsync(static_cast<char*>(HO.data_ptr()) + b0 * rb, dout[s].data_ptr(), nb * rb,
+                                cudaMemcpyDeviceToHost, d2h.stream()) == cudaSuccess,
+                "device-to-host copy failed");
+    cudaEventRecord(d2h_done[s], d2h.stream());
+  }
+  // The current stream (and with it the buffers' reuse) follows the last copies.
+  for (int i = 0; i < 2; ++i) {
+    cudaStreamWaitEvent(comp.stream(), d2h_done[i], 0);
+    cudaStreamWaitEvent(comp.stream(), h2d_done[i], 0);
+  }
+  cudaEventDestroy(start);
+  for (int i = 0; i < 2; ++i) {
+    cudaEventDestroy(h2d_done[i]);
+    cudaEventDestroy(comp_done[i]);
+    cudaEventDestroy(d2h_done[i]);
+  }
+  return HO;
+}
+
 // Reads (and clears) the device status word of `device`; raises RuntimeError
 // if a kernel since the last check reported an error.  Synchronises.
 void check_status(int64_t device) {
@@ -319,6 +439,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("return_lse") = false,
         "Attention forward with K/V of their own length and head count (GQA), an optional causal "
         "mask (bottom-right aligned) and an optional fp32 log-sum-exp [batch, heads, seq]");
+  m.def("forward_host", &forward_host, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("o") = py::none(),
+        py::arg("causal") = false, py::arg("chunks") = 0,
+        "Attention forward on host tensors: batch slices copied in, computed and copied out on three "
+        "streams so the transfers overlap each other and the compute (pinned host memory); returns O");
   m.def("check_status", &check_status, py::arg("device") = 0,
         "Raise RuntimeError if a kernel on `device` reported an error since the last check");
   m.def("_raise_formatted_error", &raise_formatted_error, py::arg("a"), py::arg("b"));
