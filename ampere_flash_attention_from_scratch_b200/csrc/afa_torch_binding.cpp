@@ -326,7 +326,10 @@ at::Tensor forward_host(const at::Tensor& HQ, const at::Tensor& HK, const at::Te
               "Flash Attention (sm_100a build) requires SM_100 (current: SM_", major, ".", minor, ")");
 
   const int64_t B = HQ.size(0);
-  const int64_t n_chunks = std::max<int64_t>(1, std::min<int64_t>(chunks > 0 ? chunks : 8, B));
+  // Default 16 slices: at [16, 8192, 32, 128] only the first slice's copy in and
+  // the last one's copy out stay exposed (63 ms per call against 58 ms for the
+  // 3.2 GB of inputs alone at 55.6 GB/s host-to-device).
+  const int64_t n_chunks = std::max<int64_t>(1, std::min<int64_t>(chunks > 0 ? chunks : 16, B));
   const int64_t per = (B + n_chunks - 1) / n_chunks;  // batches per slice
   const auto dopt = HQ.options().device(at::kCUDA, dev).pinned_memory(false);
   auto slice_shape = [&](const at::Tensor& t) {
