@@ -66,7 +66,8 @@ typedef struct AfaFwdArgs {
   int32_t* status;    /* optional device int32: 0 = ok, else an AFA_DEV_* code (see below) */
   uint64_t timeout_ns; /* bound of every device-side wait; 0 selects the default (4 s) */
   uint32_t test_flags; /* 0 in normal use; AFA_TEST_* bits below exercise failure paths */
-  /* Extensions (ABI 2.0); zero everywhere gives the reference's operation. */
+  /* Extensions (ABI 2.0: seq_len_kv, n_kv_heads, causal, lse; 3.0: sched); zero everywhere gives
+     the reference's operation. */
   int32_t seq_len_kv;  /* rows of K and V; 0 selects seq_len */
   int32_t n_kv_heads;  /* heads of K and V, a divisor of n_heads (query head h reads
                           K/V head h / (n_heads / n_kv_heads)); 0 selects n_heads */

@@ -136,4 +136,4 @@ def test_strings_and_queries():
     assert 0 < lib.afa_fwd_sm100_smem_bytes(5, 128) <= 232448
     assert lib.afa_fwd_sm100_smem_bytes(5, 96) == -1
     assert lib.afa_fwd_sm100_threads() == 384
-    assert lib.afa_sm100_version() >= 200
+    assert lib.afa_sm100_version() == 300
