@@ -126,9 +126,21 @@ struct FwdLayout {
 #define AFA_P_CHUNKS 2
 #endif
   static constexpr int kPChunks = AFA_P_CHUNKS;
-  static constexpr int kSColsPerChunk = kBN / kPChunks;       // S columns per chunk
+  static constexpr int kSColsPerChunk = kBN / kPChunks;       // S columns per chunk (even split)
   static constexpr int kPColsPerChunk = kSColsPerChunk / 2;   // TMEM columns of packed P
   static constexpr int kPvStepsPerChunk = kSColsPerChunk / 16;  // MMA K-steps per chunk
+  // Chunk c covers S columns [chunk_begin(c), chunk_begin(c + 1)).  With two
+  // chunks the split may be uneven (kPSplit): a short last chunk shortens the
+  // PV that stands between the last hand-off and the next S on the critical path.
+#ifndef AFA_P_SPLIT
+#define AFA_P_SPLIT 64
+#endif
+  static constexpr int kPSplit = AFA_P_SPLIT;
+  static_assert(kPChunks != 2 || (kPSplit % 32 == 0 && kPSplit > 0 && kPSplit < kBN),
+                "the chunk split must fall on a 32-column boundary (16 packed P columns)");
+  __host__ __device__ static constexpr int chunk_begin(int c) {
+    return kPChunks == 2 ? (c == 0 ? 0 : c == 1 ? kPSplit : kBN) : c * kSColsPerChunk;
+  }
   static constexpr int kBarPReady = kBarSFull + 2;       // [2][kPChunks]
   static constexpr int kBarOFinal = kBarPReady + 2 * kPChunks;  // [2]
   static constexpr int kBarMmaDrain = kBarOFinal + 2;
@@ -432,8 +444,8 @@ __device__ __forceinline__ void issue_pv_chunk(uint32_t d_tmem, uint32_t p_tmem,
   using L = FwdLayout<kD, kBF16, kStages>;
   constexpr uint32_t kIdesc = idesc_f16_f32(128, kD, kBF16, true);
 #pragma unroll
-  for (int i = 0; i < L::kPvStepsPerChunk; ++i) {
-    const int k = chunk * L::kPvStepsPerChunk + i;
+  for (int k = L::chunk_begin(chunk) / 16; k < L::chunk_begin(chunk + 1) / 16; ++k) {
+    const int i = k - L::chunk_begin(chunk) / 16;
     // V is MN-major (head_dim contiguous): 8-row groups 1024 B apart (SBO),
     // 64-element head_dim atoms one TMA box apart (LBO); 16 key rows per step.
     // P in TMEM: 16 elements of 16 bit = 8 columns per K step.
@@ -623,7 +635,7 @@ __device__ __forceinline__ void role_softmax(const FwdParams& p, int wg, uint32_
       // P = exp2(S * scale*log2e - m_ref) for one chunk of kSColsPerChunk columns.
       auto exp_chunk = [&](int c) {
 #pragma unroll
-        for (int k = c * L::kSColsPerChunk; k < (c + 1) * L::kSColsPerChunk; k += 2) {
+        for (int k = L::chunk_begin(c); k < L::chunk_begin(c + 1); k += 2) {
           const float2 x = __ffma2_rn(make_float2(s[k], s[k + 1]), c2, nm2);
           float2 e;
           if ((((k >> 1) * L::kEmuPairs) & 7) < L::kEmuPairs) {
@@ -650,8 +662,8 @@ __device__ __forceinline__ void role_softmax(const FwdParams& p, int wg, uint32_
       // chunk c is computed.
       auto store_chunk = [&](int c) {
 #pragma unroll
-        for (int q = 0; q < L::kPColsPerChunk; q += 16)
-          tmem_st16(tS + c * L::kPColsPerChunk + q, &pk[c * L::kPColsPerChunk + q]);
+        for (int q = L::chunk_begin(c) / 2; q < L::chunk_begin(c + 1) / 2; q += 16)
+          tmem_st16(tS + q, &pk[q]);
       };
       exp_chunk(0);
       store_chunk(0);
