@@ -11,12 +11,15 @@
 // Re-designed for sm_100a:
 //
 //   * persistent grid (one CTA per SM) walking work items (b, h, q-pair);
-//     a q-pair is 256 query rows = two 128-row Q tiles;
+//     a q-pair is 256 query rows = two 128-row Q tiles.  Items are dealt
+//     round-robin, or -- for the causal kernel given scheduler words --
+//     claimed dynamically by the producer and passed to the other warps
+//     through a small ring in shared memory (WorkQueue);
 //   * warp 0      : TMA producer.  Q0/Q1 once per work item, then K_j, V_j
 //                   into a kStages-deep ring of 128-row slots (SWIZZLE_128B);
-//   * warp 1      : MMA issuer (one thread).  S_i = Q_i K_j^T and
-//                   O_i += P_i V_j with tcgen05.mma, completion via
-//                   tcgen05.commit -> mbarrier;
+//   * warp 1      : MMA issuer (the warp computes operands, lane 0 issues).
+//                   S_i = Q_i K_j^T and O_i += P_i V_j with tcgen05.mma,
+//                   completion via tcgen05.commit -> mbarrier;
 //   * warp 2      : TMEM allocator (512 columns: S0 | S1 | O0 | O1);
 //   * warps 4-7   : softmax warpgroup 0 (Q tile 0), warps 8-11: warpgroup 1.
 //                   One thread owns one query row (one TMEM lane): row max,
