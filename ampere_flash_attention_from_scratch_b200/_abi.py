@@ -26,6 +26,7 @@ AFA_ERR_TENSOR_MAP = 7
 AFA_ERR_LAUNCH = 8
 AFA_ERR_DEVICE_TIMEOUT = 9
 AFA_ERR_TOO_LARGE = 10
+AFA_ERR_SCRATCH_LIMIT = 11
 AFA_DEV_TIMEOUT_BASE = 0x100
 AFA_NOALLOC_SCRATCH_BYTES = 256
 AFA_TEST_PRODUCER_IDLE = 1

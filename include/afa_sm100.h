@@ -41,6 +41,8 @@ extern "C" {
 #define AFA_ERR_LAUNCH 8             /* kernel launch failed */
 #define AFA_ERR_DEVICE_TIMEOUT 9     /* a device-side bounded wait ran out (status word) */
 #define AFA_ERR_TOO_LARGE 10         /* a size exceeds what the kernel indexes */
+#define AFA_ERR_SCRATCH_LIMIT 11     /* afa_fwd_sm100_noalloc: the call needs more scratch than
+                                        AFA_NOALLOC_SCRATCH_BYTES */
 
 /* Arguments of one forward call.  Strides are in elements, for the
  * (batch, seq, head) dimensions; head_dim must be contiguous (stride 1).
@@ -109,20 +111,35 @@ typedef struct AfaFwdArgs {
 int afa_fwd_sm100(const AfaFwdArgs* args, void* stream);
 
 /*
- * afa_fwd_sm100 without caller-provided scratch memory.  The only scratch any
- * call needs is the causal kernel's two scheduler words (AfaFwdArgs.sched); this
- * entry point takes them from a static, 256-byte-aligned __device__ array inside
- * the library (AFA_NOALLOC_SCRATCH_BYTES per device, located with
- * cudaGetSymbolAddress on the current device) instead, so args->sched must be
- * NULL (else AFA_ERR_INVALID_ARGUMENT), and a call needing more scratch than the
- * array holds is rejected with AFA_ERR_TOO_LARGE.  Before a causal launch it
- * clears exactly the words the kernel requires to start at zero
- * (cudaMemsetAsync on `stream`); it never allocates or frees memory.
- * Races: every call on a device shares that array, so calls that may run at the
- * same time on one device (different streams or host threads without ordering
- * between them) must not both be causal; order them on one stream, or give each
- * its own words through afa_fwd_sm100.  Otherwise identical to afa_fwd_sm100,
- * with bit-identical results.
+ * afa_fwd_sm100 for callers that must not allocate device memory.  (No
+ * counterpart in the reference, whose binding allocates through torch.)
+ *
+ * Who needs it: code that runs where cudaMalloc is off limits -- a plugin
+ * inside a host framework that owns every device allocation and forbids
+ * private ones, or a latency-critical path that cannot afford cudaMalloc's
+ * implicit device-wide synchronisation -- and so cannot hand afa_fwd_sm100
+ * the scheduler words (AfaFwdArgs.sched) the causal kernel uses as scratch.
+ *
+ * What it does instead: those words live in a static, 256-byte-aligned
+ * __device__ array inside this library, AFA_NOALLOC_SCRATCH_BYTES (256 bytes)
+ * per device, which every GPU that loads the library keeps until the process
+ * exits.  The caller still passes inputs and outputs; args->sched must be NULL
+ * (else AFA_ERR_INVALID_ARGUMENT), and a call that would need more scratch
+ * than the array holds is refused with AFA_ERR_SCRATCH_LIMIT (today a call
+ * needs at most 8 bytes).  Nothing is allocated or freed: before each causal
+ * launch the entry point clears, with cudaMemsetAsync on `stream`, exactly the
+ * words that must start at zero, because the array keeps whatever the previous
+ * call left in it.
+ *
+ * Set-up: the first causal call on a device looks up the array's device
+ * address (cudaGetSymbolAddress, with that device current); make that first
+ * call before any stream capture on the device.
+ *
+ * Races: every call on a device shares the array, so two causal calls whose
+ * kernels may overlap on the GPU (different streams, or threads with no
+ * ordering between them) corrupt each other's schedule; order them on one
+ * stream, or give each its own words through afa_fwd_sm100.  Otherwise the
+ * same as afa_fwd_sm100, with bit-identical results.
  */
 #define AFA_NOALLOC_SCRATCH_BYTES 256
 int afa_fwd_sm100_noalloc(const AfaFwdArgs* args, void* stream);

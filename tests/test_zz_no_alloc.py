@@ -1,8 +1,14 @@
-"""afa_fwd_sm100_noalloc: the entry point whose scratch memory (the causal
-kernel's scheduler words) comes from a static __device__ array in the library
-instead of the caller.  Checked against the existing entry point
-(afa_fwd_sm100 with caller-owned words) on two consecutive calls: results must
-be bit-identical, and the static words are reused from one call to the next."""
+"""afa_fwd_sm100_noalloc, the entry point for callers that may not allocate
+device memory (a plugin whose host owns every allocation, or a path that
+cannot take cudaMalloc's synchronisation): the causal kernel's scheduler words
+come from a static __device__ array in the library instead of the caller.
+
+Checked against the existing entry point (afa_fwd_sm100 with caller-owned
+words) on two consecutive calls: results must be bit-identical (tighter than
+the fp16/bf16 tolerances of the other tests), and the static words, which keep
+the previous call's contents, are reused from one call to the next.  The file
+is named to be collected last, so a run that stops at the first failure has
+run every other test first."""
 
 import ctypes
 
@@ -37,6 +43,9 @@ def test_exported_and_rejects_caller_words_without_gpu():
         a = _valid_args(**over)
         assert lib.afa_fwd_sm100_noalloc(ctypes.byref(a), None) == code == lib.afa_fwd_sm100(ctypes.byref(a), None)
     assert lib.afa_fwd_sm100_noalloc(None, None) == _abi.AFA_ERR_INVALID_ARGUMENT
+    # A request beyond the static array has its own, explicit error text.
+    assert "AFA_NOALLOC_SCRATCH_BYTES" in _abi.strerror(_abi.AFA_ERR_SCRATCH_LIMIT)
+    assert _abi.AFA_NOALLOC_SCRATCH_BYTES == 256
 
 
 def _inputs(B, N, NK, H, HK, d, seed):
