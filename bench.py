@@ -90,7 +90,7 @@ def load_traffic(workload: str):
 
 class ClockSampler:
     """SM clock, power and clock-event (throttle) reasons of one GPU, sampled
-    every 50 ms during the run with the time of each sample.
+    every 10 ms during the run with the time of each sample.
 
     Reads NVML directly (the source nvidia-smi prints from); nvidia-smi through
     a pipe is block-buffered, so its lines cannot be matched to the timed
@@ -131,7 +131,7 @@ class ClockSampler:
                     break
                 names = [n for b, n in self.REASONS.items() if bits & b]
                 self.samples.append((t, float(mhz), float(max_mhz), watts, names))
-                time.sleep(0.05)
+                time.sleep(0.01)
 
         self.thread = threading.Thread(target=run, daemon=True)
         self.thread.start()
@@ -169,16 +169,23 @@ class ClockSampler:
         if self.thread is not None:
             self.thread.join(timeout=2)
 
-    def summary(self, windows):
+    def summary(self, windows, pad_s: float = 0.1):
         """Median SM clock and power, max clock and every reason seen, over the
-        samples that fall inside any of the (t0, t1) windows."""
+        samples that fall inside any of the (t0, t1) windows.  A window too
+        short to hold a sample (a few ms on many GPUs) is widened by pad_s on
+        both sides, and the result says so."""
         sel = [x for x in self.samples if any(t0 <= x[0] <= t1 for t0, t1 in windows)]
+        widened = False
+        if not sel and pad_s > 0:
+            sel = [x for x in self.samples if any(t0 - pad_s <= x[0] <= t1 + pad_s for t0, t1 in windows)]
+            widened = bool(sel)
         if not sel:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
         reasons = sorted({n for x in sel for n in x[4]})
         return {"sm_mhz": statistics.median(x[1] for x in sel), "sm_max_mhz": max(x[2] for x in sel),
                 "power_w": round(statistics.median(x[3] for x in sel), 1), "reasons": reasons,
-                "samples": len(sel), "source": "nvml" if self.proc is None else "nvidia-smi"}
+                "samples": len(sel), "source": "nvml" if self.proc is None else "nvidia-smi",
+                **({"window_widened_s": pad_s} if widened else {})}
 
 
 def cpu_attention_rate(wl: Workload, budget_s: float, max_slices: int = 64, causal: bool = False):

@@ -20,6 +20,10 @@ def test_clock_summary_uses_only_samples_inside_windows():
     assert out["reasons"] == ["sw_power_cap"]
     assert out["power_w"] == 982.5
     assert s.summary([(10.0, 11.0)])["samples"] == 0
+    # a window shorter than the sampling period takes the samples just around it
+    near = s.summary([(2.24, 2.26)], pad_s=0.1)
+    assert near["samples"] == 2 and near["window_widened_s"] == 0.1
+    assert s.summary([(2.24, 2.26)], pad_s=0.0)["samples"] == 0
 
 
 def test_visible_devices_mapping(monkeypatch):
