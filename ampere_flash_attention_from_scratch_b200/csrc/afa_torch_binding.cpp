@@ -347,16 +347,20 @@ at::Tensor forward_host(const at::Tensor& HQ, const at::Tensor& HK, const at::Te
   c10::cuda::CUDAStream comp = at::cuda::getCurrentCUDAStream();
   c10::cuda::CUDAStream h2d = c10::cuda::getStreamFromPool(false, static_cast<c10::DeviceIndex>(dev));
   c10::cuda::CUDAStream d2h = c10::cuda::getStreamFromPool(false, static_cast<c10::DeviceIndex>(dev));
-  cudaEvent_t start, h2d_done[2], comp_done[2], d2h_done[2];
-  auto mk = [](cudaEvent_t* e) {
-    TORCH_CHECK(cudaEventCreateWithFlags(e, cudaEventDisableTiming) == cudaSuccess, "cudaEventCreate failed");
+  // Events destroyed on every exit path, including an error thrown mid-loop.
+  struct Event {
+    cudaEvent_t e = nullptr;
+    Event() {
+      TORCH_CHECK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming) == cudaSuccess, "cudaEventCreate failed");
+    }
+    ~Event() {
+      if (e != nullptr) cudaEventDestroy(e);
+    }
+    Event(const Event&) = delete;
+    Event& operator=(const Event&) = delete;
+    operator cudaEvent_t() const { return e; }
   };
-  mk(&start);
-  for (int i = 0; i < 2; ++i) {
-    mk(&h2d_done[i]);
-    mk(&comp_done[i]);
-    mk(&d2h_done[i]);
-  }
+  Event start, h2d_done[2], comp_done[2], d2h_done[2];
   // The buffers were taken from the current stream's pool: earlier work on it
   // completes before the copy stream writes them.
   cudaEventRecord(start, comp.stream());
@@ -397,12 +401,6 @@ at::Tensor forward_host(const at::Tensor& HQ, const at::Tensor& HK, const at::Te
   for (int i = 0; i < 2; ++i) {
     cudaStreamWaitEvent(comp.stream(), d2h_done[i], 0);
     cudaStreamWaitEvent(comp.stream(), h2d_done[i], 0);
-  }
-  cudaEventDestroy(start);
-  for (int i = 0; i < 2; ++i) {
-    cudaEventDestroy(h2d_done[i]);
-    cudaEventDestroy(comp_done[i]);
-    cudaEventDestroy(d2h_done[i]);
   }
   return HO;
 }
