@@ -25,6 +25,7 @@
 // with K/V of their own length and head count (GQA), the causal mask and the
 // fp32 log-sum-exp [batch, heads, seq] (None unless return_lse).
 #include <ATen/cuda/CUDAContext.h>
+#include <ATen/cuda/CachingHostAllocator.h>
 #include <c10/cuda/CUDAStream.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <cuda_runtime.h>
@@ -71,11 +72,13 @@ int dtype_code(const at::Tensor& t) {
   return -1;
 }
 
-// One persistent device status word per device (int32, zero = ok).
+// One persistent device status word per device (int32, zero = ok).  Handed out
+// by value: another thread's first call on a higher device index resizes the
+// vector, which would leave a reference into it dangling.
 std::mutex g_status_mu;
 std::vector<at::Tensor> g_status;
 
-at::Tensor& status_word(const at::Device& dev) {
+at::Tensor status_word(const at::Device& dev) {
   std::lock_guard<std::mutex> lock(g_status_mu);
   const size_t i = static_cast<size_t>(dev.index());
   if (g_status.size() <= i) g_status.resize(i + 1);
@@ -96,7 +99,7 @@ int32_t* sched_words(const at::Device& dev, cudaStream_t stream) {
 }
 
 int32_t read_and_clear_status(const at::Device& dev) {
-  at::Tensor& s = status_word(dev);
+  at::Tensor s = status_word(dev);
   const int32_t v = s.item<int32_t>();
   if (v != 0) {
     s.zero_();
@@ -190,8 +193,7 @@ float launch(const at::Tensor& TQ, const at::Tensor& TK, const at::Tensor& TV, c
   args.head_dim = static_cast<int32_t>(TQ.size(3));
   args.dtype = dt;
   args.scale = scale;
-  at::Tensor& status = status_word(TQ.device());
-  args.status = status.data_ptr<int32_t>();
+  args.status = status_word(TQ.device()).data_ptr<int32_t>();
   args.timeout_ns = 0;
   args.seq_len_kv = static_cast<int32_t>(TK.size(1));
   args.n_kv_heads = static_cast<int32_t>(TK.size(2));
@@ -402,6 +404,21 @@ at::Tensor forward_host(const at::Tensor& HQ, const at::Tensor& HK, const at::Te
     cudaStreamWaitEvent(comp.stream(), d2h_done[i], 0);
     cudaStreamWaitEvent(comp.stream(), h2d_done[i], 0);
   }
+  // The copies are still in flight when this returns.  Page-locked tensors from
+  // torch's host allocator are told which stream uses them, so a caller that drops
+  // them now (q.pin_memory() passed as a temporary) does not get their memory
+  // handed to a new tensor before the copies have read or written it -- what
+  // torch's own non-blocking copy_ does.  Pageable memory needs nothing: the
+  // runtime stages it before cudaMemcpyAsync returns.
+  auto keep_until_copied = [](const at::Tensor& t, const c10::cuda::CUDAStream& s) {
+    if (t.is_pinned())
+      at::getHostAllocator(at::kCUDA)->record_event(t.storage().mutable_data(),
+                                                    t.storage().data_ptr().get_context(), s.unwrap());
+  };
+  keep_until_copied(HQ, h2d);
+  keep_until_copied(HK, h2d);
+  keep_until_copied(HV, h2d);
+  keep_until_copied(HO, d2h);
   return HO;
 }
 

@@ -48,3 +48,26 @@ def test_rejects_device_tensors():
     q = torch.randn(1, 128, 2, 64, dtype=torch.float16, device="cuda")
     with pytest.raises(RuntimeError, match="host"):
         fa.forward_host(q, q, q)
+
+
+def test_temporary_pinned_inputs_survive_until_copied():
+    """Inputs passed as temporaries (``q.pin_memory()``) are released when the call
+    returns, while their copies are still queued behind earlier work on the stream.
+    Page-locked tensors allocated right after (and filled with NaN) must not be
+    given that memory before the copies have read it."""
+    B, N, H, d = 8, 4096, 16, 128
+    q, k, v = _host(B, N, N, H, H, d, torch.float16, seed=11, pinned=False)
+    # Three page-locked blocks of this size left in the allocator's cache: the
+    # temporaries below take them without page-locking anew (fast), so the call
+    # is made while the spin still holds its copies back.
+    warm = [torch.empty_like(q).pin_memory() for _ in range(3)]
+    del warm
+    torch.cuda.synchronize()
+    torch.cuda._sleep(2_000_000_000)  # a fixed-length spin (~1 s) keeps the copies queued
+    o = fa.forward_host(q.pin_memory(), k.pin_memory(), v.pin_memory())
+    junk = [torch.full_like(q, float("nan")).pin_memory() for _ in range(3)]
+    torch.cuda.synchronize()
+    fa.check_status(0)
+    ref, _ = fa.forward_ext(q.cuda(), k.cuda(), v.cuda())
+    assert torch.equal(o, ref.cpu())
+    del junk
