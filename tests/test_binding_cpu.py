@@ -34,3 +34,38 @@ def test_package_exports_forward():
     import ampere_flash_attention_from_scratch_b200 as pkg
 
     assert pkg.forward is fa.forward
+
+
+def test_forward_ext_rejects_host_tensors():
+    q = torch.randn(1, 128, 2, 64, dtype=torch.float16)
+    with pytest.raises(RuntimeError, match="must be a CUDA tensor"):
+        fa.forward_ext(q, q, q)
+
+
+def _h(*shape, dtype=torch.float16):
+    return torch.zeros(*shape, dtype=dtype)
+
+
+@pytest.mark.parametrize("args,match", [
+    ((_h(1, 64, 2, 64).transpose(1, 2), _h(1, 64, 2, 64), _h(1, 64, 2, 64)), "contiguous"),
+    ((_h(1, 64, 2, 64, dtype=torch.float32),) * 3, "Only fp16 and bf16"),
+    ((_h(1, 64, 2, 64), _h(1, 64, 2, 64, dtype=torch.bfloat16), _h(1, 64, 2, 64)), "same data type"),
+    ((_h(1, 64, 2, 64), _h(1, 64, 2, 64), _h(1, 32, 2, 64)), "key and value tensors must have the same shape"),
+    ((_h(1, 64, 2, 64), _h(2, 64, 2, 64), _h(2, 64, 2, 64)), "batch / head_dim differ"),
+    ((_h(1, 64, 3, 64), _h(1, 64, 2, 64), _h(1, 64, 2, 64)), "multiple of the number of key/value heads"),
+    ((_h(1, 64, 2, 96),) * 3, "no sm_100a kernel for head_dim"),
+    ((_h(1, 0, 2, 64),) * 3, "must be positive"),
+])
+def test_forward_host_rejects_before_any_cuda_call(args, match):
+    """forward_host checks its host tensors before touching the device, so the
+    same messages appear on a machine without a GPU."""
+    with pytest.raises(RuntimeError, match=match):
+        fa.forward_host(*args)
+
+
+def test_forward_host_rejects_a_mismatched_output():
+    q = _h(1, 64, 2, 64)
+    with pytest.raises(RuntimeError, match="o must be a contiguous host tensor"):
+        fa.forward_host(q, q, q, _h(1, 64, 2, 32))
+    with pytest.raises(RuntimeError, match="o must be a contiguous host tensor"):
+        fa.forward_host(q, q, q, _h(1, 64, 2, 64, dtype=torch.bfloat16))
