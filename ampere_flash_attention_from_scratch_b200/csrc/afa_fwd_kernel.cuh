@@ -369,6 +369,48 @@ __device__ __forceinline__ void role_load(const FwdParams& p, uint32_t sbase, ui
     decode_work<kCausal>(p, w, qp, h, b);
     const int h_kv = p.kv_group == 1 ? h : h / p.kv_group;
     const int n_tiles = kv_tiles<kCausal>(p, qp, 1);
+    if constexpr (!kCausal) {
+      // Unmasked items load K_0, Q0, V_0, Q1, K_1, V_1, ...: K_0 needs only a
+      // ring slot, which the previous item freed a tile earlier, while Q1's
+      // buffer frees only once that item's last S1 has run, so the first K
+      // tile's DRAM latency overlaps the end of the previous item.  (Causal
+      // items keep Q first: their Q tile 0 finishes early and frees its buffer
+      // before the ring slot frees.)  The ring order is the same either way.
+      auto load_q = [&](int t) -> bool {
+        if (!sy.wait(bar(L::kBarQEmpty + t), (it & 1u) ^ 1u, kSiteLoadQEmpty)) return false;
+        if (leader) mbar_arrive_expect_tx(bar(L::kBarQFull + t), L::kTileBytes);
+        const bool si = (p.seq_inner_mask & 1u) != 0u;
+#pragma unroll
+        for (int a = 0; a < L::kAtoms; ++a) {
+          const int row0 = qp * 256 + t * 128;
+          if (leader)
+            tma_load_4d(sbase + L::kOffQ + t * L::kTileBytes + a * L::kAtomBytes, &p.tm_q,
+                        bar(L::kBarQFull + t), a * 64, si ? row0 : h, si ? h : row0, b, pol_q);
+        }
+        ++q_cnt[t];
+        return true;
+      };
+      auto load_kv = [&](int j, int kv) -> bool {
+        const uint32_t slot = kv_cnt % kStages;
+        const uint32_t ph = (kv_cnt / kStages) & 1u;
+        if (!sy.wait(bar(L::kBarKVEmpty + slot), ph ^ 1u, kSiteLoadKVEmpty)) return false;
+        if (leader) mbar_arrive_expect_tx(bar(L::kBarKVFull + slot), L::kTileBytes);
+        const CUtensorMap* map = kv ? &p.tm_v : &p.tm_k;
+        const bool si = (p.seq_inner_mask & (kv ? 4u : 2u)) != 0u;
+#pragma unroll
+        for (int a = 0; a < L::kAtoms; ++a) {
+          if (leader)
+            tma_load_4d(sbase + L::kOffKV + slot * L::kTileBytes + a * L::kAtomBytes, map,
+                        bar(L::kBarKVFull + slot), a * 64, si ? j * 128 : h_kv, si ? h_kv : j * 128, b, pol_kv);
+        }
+        ++kv_cnt;
+        return true;
+      };
+      ok = load_kv(0, 0) && load_q(0) && load_kv(0, 1) && load_q(1);
+      for (int j = 1; j < n_tiles && ok; ++j) ok = load_kv(j, 0) && load_kv(j, 1);
+      if (!ok) break;
+      continue;
+    }
 #pragma unroll
     for (int t = 0; t < 2; ++t) {
       if (!sy.wait(bar(L::kBarQEmpty + t), (it & 1u) ^ 1u, kSiteLoadQEmpty)) { ok = false; break; }
