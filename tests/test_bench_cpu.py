@@ -1,5 +1,6 @@
-"""bench.py helpers that need no GPU: the clock summary over timed windows,
-the traffic table and the peaks fallback."""
+"""bench.py parts that need no GPU: the clock summary over timed windows, the
+traffic table, the peaks fallback, and the reference arm (the CPU path on rank
+0, the other ranks exiting without work)."""
 
 import bench
 
@@ -38,3 +39,43 @@ def test_traffic_table_and_peaks():
     assert bench.load_traffic("no-such-workload") is None
     peaks, source = bench.load_peaks()
     assert peaks["bf16_tflops"] > 0 and source in ("measured", "fallback")
+
+
+def _bench(args, rank):
+    import os
+    import subprocess
+    import sys
+    from pathlib import Path
+
+    root = Path(__file__).resolve().parents[1]
+    env = dict(os.environ, RANK=str(rank), LOCAL_RANK=str(rank), WORLD_SIZE="2")
+    return subprocess.run([sys.executable, str(root / "bench.py"), *args], cwd=root, env=env,
+                          capture_output=True, text=True, timeout=300)
+
+
+def test_reference_arm_rank0_prints_one_line_other_ranks_exit_quietly():
+    import json
+
+    args = ["--impl", "reference", "--config", "cfg1", "--gpus", "2", "--steps", "1"]
+    r1 = _bench(args, rank=1)
+    assert r1.returncode == 0 and r1.stdout.strip() == "", r1.stderr[-2000:]
+    r0 = _bench(args, rank=0)
+    assert r0.returncode == 0, r0.stderr[-2000:]
+    lines = [ln for ln in r0.stdout.splitlines() if ln.strip()]
+    assert len(lines) == 1
+    line = json.loads(lines[0])
+    assert line["impl"] == "reference" and line["unit"] == "TFLOP/s" and line["value"] > 0
+    assert line["warmup"] >= 3 and line["steps"] == 1 and line["n_gpus"] == 2
+    assert line["cpu_baseline"]["kind"] == "port" and line["cpu_baseline"]["value"] == line["value"]
+    assert line["e2e"] == {"value": line["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
+                           "d2h_bytes_per_step": 0}
+    assert line["config"]["workload"] == "cfg1"
+
+
+def test_reference_arm_has_no_causal_mask():
+    import json
+
+    r = _bench(["--impl", "reference", "--config", "cfg1", "--causal"], rank=0)
+    assert r.returncode == 0
+    line = json.loads(r.stdout.strip().splitlines()[-1])
+    assert line["impl"] == "reference" and "unavailable" in line
