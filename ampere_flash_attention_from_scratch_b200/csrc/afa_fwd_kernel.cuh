@@ -15,8 +15,9 @@
 //     round-robin, or -- for the causal kernel given scheduler words --
 //     claimed dynamically by the producer and passed to the other warps
 //     through a small ring in shared memory (WorkQueue);
-//   * warp 0      : TMA producer.  Q0/Q1 once per work item, then K_j, V_j
+//   * warp 0      : TMA producer.  Q0/Q1 once per work item and K_j, V_j
 //                   into a kStages-deep ring of 128-row slots (SWIZZLE_128B);
+//                   an unmasked item's first K tile goes ahead of its Q tiles;
 //   * warp 1      : MMA issuer (the warp computes operands, lane 0 issues).
 //                   S_i = Q_i K_j^T and O_i += P_i V_j with tcgen05.mma,
 //                   completion via tcgen05.commit -> mbarrier;
