@@ -31,6 +31,7 @@ AFA_DEV_TIMEOUT_BASE = 0x100
 AFA_NOALLOC_SCRATCH_BYTES = 256
 AFA_TEST_PRODUCER_IDLE = 1
 AFA_TEST_MMA_IDLE = 2
+AFA_TEST_KEEP_SCHED = 4
 
 # Every extern "C" symbol declared in include/afa_sm100.h.
 EXPORTED_SYMBOLS = (

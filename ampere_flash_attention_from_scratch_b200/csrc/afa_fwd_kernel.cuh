@@ -84,7 +84,8 @@ struct FwdParams {
   int* status;
   unsigned long long timeout_ns;
   unsigned test_flags;  // bit 0: the producer issues no loads; bit 1: the MMA issuer issues nothing
-                        // (both exercise the timeout path; bit 1 with loads in flight)
+                        // (both exercise the timeout path; bit 1 with loads in flight);
+                        // bit 2: the last CTA leaves the scheduler words non-zero
 };
 
 // Bounded-wait sites, reported as AFA_DEV_TIMEOUT_BASE + site.
@@ -196,6 +197,17 @@ struct CtaSync {
     return wait_slow(bar, parity, site, true);
   }
 
+  // Records an error code in the status word.  The word may be device memory
+  // or mapped page-locked host memory (a host can then read it without
+  // synchronising), so it is written with plain stores, not an atomic: when
+  // several waits run out, one of their codes remains.
+  __device__ __forceinline__ void report(int code) const {
+    if (status == nullptr) return;
+    volatile int* s = status;
+    if (*s == 0) *s = code;
+    __threadfence_system();
+  }
+
   // honour_abort = false is used by teardown drains, which must run to the end.
   // Waiting threads are suspended by the hardware between checks (up to
   // kSuspendNs each), so idle warps do not take issue slots from the warps
@@ -210,7 +222,7 @@ struct CtaSync {
       const uint64_t dt = globaltimer_ns() - t0;
       if (dt > timeout_ns || it > (1u << 30)) {
         *abort_flag = 1;
-        if (status != nullptr) atomicCAS(status, 0, AFA_DEV_TIMEOUT_BASE + site);
+        report(AFA_DEV_TIMEOUT_BASE + site);
         return false;
       }
     }
@@ -281,6 +293,7 @@ struct WorkQueue {
   volatile int* slots;    // [kSlots]
   uint32_t full0, empty0; // item_full / item_empty barriers
   int n_work;
+  bool keep_words;        // test only: the last CTA does not reset the words
   static constexpr int kDone = -1;   // no more items
   static constexpr int kAbort = -2;  // a bounded wait ran out
 
@@ -323,7 +336,7 @@ struct WorkQueue {
   __device__ __forceinline__ void finish() const {
     if (!dynamic() || (threadIdx.x & 31u) != 0u) return;
     __threadfence();
-    if (atomicAdd(sched + 1, 1) == static_cast<int>(gridDim.x) - 1) {
+    if (atomicAdd(sched + 1, 1) == static_cast<int>(gridDim.x) - 1 && !keep_words) {
       atomicExch(sched, 0);
       atomicExch(sched + 1, 0);
     }
@@ -800,7 +813,8 @@ __global__ void __launch_bounds__(384, 1) afa_fwd_sm100_kernel(const __grid_cons
   // only with caller-provided scheduler words.
   const WorkQueue<L::kItemSlots> wq{kCausal ? p.sched : nullptr,
                                     reinterpret_cast<volatile int*>(smem + L::kOffItems),
-                                    bar0 + 8u * L::kBarItemFull, bar0 + 8u * L::kBarItemEmpty, p.n_work};
+                                    bar0 + 8u * L::kBarItemFull, bar0 + 8u * L::kBarItemEmpty, p.n_work,
+                                    (p.test_flags & 4u) != 0u};
 
   if (warp < 4) {
     setmaxnreg_dec<L::kProducerRegs>();

@@ -17,7 +17,9 @@
 //   * `o` is checked against q's shape (the reference compared q with v);
 //   * with benchmark=False the returned runtime is 0.0 (the reference returned
 //     an uninitialised float); with benchmark=True the events are destroyed
-//     and the device status word is checked.
+//     and the launch's own status is checked after it finishes;
+//   * every call first raises if an earlier launch on its device reported a
+//     device-side abort (the reference checked nothing after its launch).
 //
 // One function beyond the reference:
 //     O, lse = afa_flash_attention_kernels.forward_ext(q, k, v, o=None, causal=False,
@@ -72,23 +74,57 @@ int dtype_code(const at::Tensor& t) {
   return -1;
 }
 
-// One persistent device status word per device (int32, zero = ok).  Handed out
-// by value: another thread's first call on a higher device index resizes the
-// vector, which would leave a reference into it dangling.
+// One status word per device (int32, zero = ok) in mapped page-locked host
+// memory: every launch on the device gets its device address, a kernel whose
+// bounded wait runs out stores its code there, and the host reads it without
+// synchronising.  Each call first takes (and clears) what earlier launches on
+// its device reported, so a device-side abort is raised by the next call on
+// that device -- at the latest by the first one made after the aborted launch
+// has finished -- or by check_status(), which synchronises first.  Kept until
+// the process exits (4 bytes of page-locked memory per device).
+struct StatusWord {
+  int32_t* host = nullptr;    // what the host reads
+  int32_t* device = nullptr;  // the same word as the kernel addresses it
+};
 std::mutex g_status_mu;
-std::vector<at::Tensor> g_status;
+std::map<int, StatusWord> g_status;
 
-at::Tensor status_word(const at::Device& dev) {
+StatusWord status_word(int dev) {
   std::lock_guard<std::mutex> lock(g_status_mu);
-  const size_t i = static_cast<size_t>(dev.index());
-  if (g_status.size() <= i) g_status.resize(i + 1);
-  if (!g_status[i].defined())
-    g_status[i] = at::zeros({1}, at::TensorOptions().dtype(at::kInt).device(dev));
-  return g_status[i];
+  StatusWord& w = g_status[dev];
+  if (w.host == nullptr) {
+    void* h = nullptr;
+    void* d = nullptr;
+    TORCH_CHECK(cudaHostAlloc(&h, sizeof(int32_t), cudaHostAllocMapped | cudaHostAllocPortable) == cudaSuccess,
+                "cudaHostAlloc of the status word failed");
+    *static_cast<volatile int32_t*>(h) = 0;
+    if (cudaHostGetDevicePointer(&d, h, 0) != cudaSuccess) {
+      cudaFreeHost(h);
+      TORCH_CHECK(false, "the device cannot address mapped host memory (status word)");
+    }
+    w.host = static_cast<int32_t*>(h);
+    w.device = static_cast<int32_t*>(d);
+  }
+  return w;
+}
+
+// Takes the code earlier launches on `dev` left in the status word and clears it.
+int32_t take_status(int dev) {
+  return __atomic_exchange_n(status_word(dev).host, 0, __ATOMIC_ACQ_REL);
+}
+
+// Raises for an abort that a launch made before this call reported.
+void raise_earlier_abort(int dev) {
+  const int32_t st = take_status(dev);
+  TORCH_CHECK(st == 0, "attention kernel reported (an earlier launch on cuda:", dev, "): ", afa_status_string(st));
 }
 
 // Scheduler words of the causal kernel (AfaFwdArgs.sched), one pair per
-// (device, stream) so launches that may overlap never share them; zero at rest.
+// (device, stream) so launches that may overlap never share them; zero at rest
+// (the kernel returns them to zero when it ends, also after an abort).  A CUDA
+// graph captured on a stream keeps that stream's pair: replays of it must be
+// ordered with every other causal launch made on the capture stream, and two
+// such graphs must not be replayed at the same time.
 std::map<std::pair<int, cudaStream_t>, at::Tensor> g_sched;
 
 int32_t* sched_words(const at::Device& dev, cudaStream_t stream) {
@@ -98,18 +134,11 @@ int32_t* sched_words(const at::Device& dev, cudaStream_t stream) {
   return t.data_ptr<int32_t>();
 }
 
-int32_t read_and_clear_status(const at::Device& dev) {
-  at::Tensor s = status_word(dev);
-  const int32_t v = s.item<int32_t>();
-  if (v != 0) {
-    s.zero_();
-    // A kernel that stopped early may not have returned its scheduler words to zero.
-    std::lock_guard<std::mutex> lock(g_status_mu);
-    for (auto& kv : g_sched)
-      if (kv.first.first == static_cast<int>(dev.index())) kv.second.zero_();
-  }
-  return v;
-}
+// Test hook: AFA_TEST_* flags and a wait bound for the next launch only
+// (drives the kernel's bounded-wait abort through this binding).
+std::mutex g_test_mu;
+uint32_t g_test_flags = 0;
+uint64_t g_test_timeout_ns = 0;
 
 float launch(const at::Tensor& TQ, const at::Tensor& TK, const at::Tensor& TV, const at::Tensor& TO,
              int dt, float scale, bool causal, float* lse, bool benchmark);
@@ -134,6 +163,7 @@ std::tuple<at::Tensor, double> flash_attention_forward(const py::object& py_cfg,
   TORCH_CHECK(major == 10 && minor == 0,
               "Flash Attention (sm_100a build) requires SM_100 (current: SM_", major, ".", minor,
               ")");
+  raise_earlier_abort(dev);
 
   const int dt = dtype_code(TQ);
   TORCH_CHECK(dt > 0, "Only fp16 and bf16 are supported");
@@ -193,8 +223,14 @@ float launch(const at::Tensor& TQ, const at::Tensor& TK, const at::Tensor& TV, c
   args.head_dim = static_cast<int32_t>(TQ.size(3));
   args.dtype = dt;
   args.scale = scale;
-  args.status = status_word(TQ.device()).data_ptr<int32_t>();
-  args.timeout_ns = 0;
+  args.status = status_word(TQ.device().index()).device;
+  {
+    std::lock_guard<std::mutex> lock(g_test_mu);
+    args.test_flags = g_test_flags;
+    args.timeout_ns = g_test_timeout_ns;
+    g_test_flags = 0;
+    g_test_timeout_ns = 0;
+  }
   args.seq_len_kv = static_cast<int32_t>(TK.size(1));
   args.n_kv_heads = static_cast<int32_t>(TK.size(2));
   args.causal = causal ? 1 : 0;
@@ -218,8 +254,8 @@ float launch(const at::Tensor& TQ, const at::Tensor& TK, const at::Tensor& TV, c
     cudaEventDestroy(stop);
   }
   TORCH_CHECK(rc == AFA_OK, "afa_fwd_sm100 failed: ", afa_strerror(rc));
-  if (benchmark) {
-    const int32_t st = read_and_clear_status(TQ.device());
+  if (benchmark) {  // the launch has finished: its own status is in the word
+    const int32_t st = take_status(TQ.device().index());
     TORCH_CHECK(st == 0, "attention kernel reported: ", afa_status_string(st));
   }
   return runtime;
@@ -245,6 +281,7 @@ std::tuple<at::Tensor, std::optional<at::Tensor>> forward_ext(
   TORCH_CHECK(major == 10 && minor == 0,
               "Flash Attention (sm_100a build) requires SM_100 (current: SM_", major, ".", minor,
               ")");
+  raise_earlier_abort(dev);
   const int dt = dtype_code(TQ);
   TORCH_CHECK(dt > 0, "Only fp16 and bf16 are supported");
   TORCH_CHECK(TK.dtype() == TQ.dtype() && TV.dtype() == TQ.dtype(),
@@ -317,6 +354,9 @@ at::Tensor forward_host(const at::Tensor& HQ, const at::Tensor& HK, const at::Te
     HO = out_.value();
     TORCH_CHECK(HO.device().is_cpu() && HO.is_contiguous() && HO.sizes() == HQ.sizes() && HO.dtype() == HQ.dtype(),
                 "o must be a contiguous host tensor shaped and typed like q");
+    // A copy into pageable memory returns only when it has finished, which
+    // would hold each slice's copy in behind the previous slice's kernel.
+    TORCH_CHECK(HO.is_pinned(), "o must be page-locked (pin_memory()) so its copies overlap the compute");
   } else {
     HO = at::empty(HQ.sizes(), HQ.options().pinned_memory(true));
   }
@@ -326,6 +366,7 @@ at::Tensor forward_host(const at::Tensor& HQ, const at::Tensor& HK, const at::Te
   cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
   TORCH_CHECK(major == 10 && minor == 0,
               "Flash Attention (sm_100a build) requires SM_100 (current: SM_", major, ".", minor, ")");
+  raise_earlier_abort(dev);
 
   const int64_t B = HQ.size(0);
   // Default 16 slices: at [16, 8192, 32, 128] only the first slice's copy in and
@@ -422,13 +463,23 @@ at::Tensor forward_host(const at::Tensor& HQ, const at::Tensor& HK, const at::Te
   return HO;
 }
 
-// Reads (and clears) the device status word of `device`; raises RuntimeError
-// if a kernel since the last check reported an error.  Synchronises.
+// Waits for all work on `device`, then takes (and clears) its status word;
+// raises RuntimeError if a kernel since the last check reported an error.
 void check_status(int64_t device) {
   const at::Device dev(at::kCUDA, static_cast<c10::DeviceIndex>(device));
   c10::cuda::CUDAGuard g{dev};
-  const int32_t st = read_and_clear_status(dev);
+  TORCH_CHECK(cudaDeviceSynchronize() == cudaSuccess, "cudaDeviceSynchronize failed");
+  const int32_t st = take_status(static_cast<int>(device));
   TORCH_CHECK(st == 0, "attention kernel reported: ", afa_status_string(st));
+}
+
+// Test hook: the next launch of this module runs with these AFA_TEST_* flags
+// and wait bound (nanoseconds, 0 = default); later launches are normal again.
+void set_test_flags(int64_t flags, int64_t timeout_ns) {
+  TORCH_CHECK(flags >= 0 && timeout_ns >= 0, "flags and timeout_ns must be non-negative");
+  std::lock_guard<std::mutex> lock(g_test_mu);
+  g_test_flags = static_cast<uint32_t>(flags);
+  g_test_timeout_ns = static_cast<uint64_t>(timeout_ns);
 }
 
 std::vector<std::tuple<int, int>> kernel_keys() {
@@ -462,7 +513,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "Attention forward on host tensors: batch slices copied in, computed and copied out on three "
         "streams so the transfers overlap each other and the compute (pinned host memory); returns O");
   m.def("check_status", &check_status, py::arg("device") = 0,
-        "Raise RuntimeError if a kernel on `device` reported an error since the last check");
+        "Wait for `device`, then raise RuntimeError if a kernel on it reported an error since the last check");
+  m.def("_set_test_flags", &set_test_flags, py::arg("flags"), py::arg("timeout_ns") = 0,
+        "Test hook: AFA_TEST_* flags and wait bound for the next launch only");
   m.def("_raise_formatted_error", &raise_formatted_error, py::arg("a"), py::arg("b"));
   m.def("kernel_keys", &kernel_keys, "(dtype code, d_head) pairs with a compiled sm_100a kernel");
 }

@@ -65,7 +65,9 @@ typedef struct AfaFwdArgs {
   int32_t head_dim;   /* 64 or 128 */
   int32_t dtype;      /* AFA_DTYPE_FP16 or AFA_DTYPE_BF16 */
   float scale;        /* softmax scale; <= 0 selects 1/sqrt(head_dim) as the reference */
-  int32_t* status;    /* optional device int32: 0 = ok, else an AFA_DEV_* code (see below) */
+  int32_t* status;    /* optional int32 the kernel can address -- device memory, or mapped
+                          page-locked host memory (cudaHostAllocMapped) so the host can read
+                          it without synchronising: 0 = ok, else an AFA_DEV_* code (see below) */
   uint64_t timeout_ns; /* bound of every device-side wait; 0 selects the default (4 s) */
   uint32_t test_flags; /* 0 in normal use; AFA_TEST_* bits below exercise failure paths */
   /* Extensions (ABI 2.0: seq_len_kv, n_kv_heads, causal, lse; 3.0: sched); zero everywhere gives
@@ -99,6 +101,10 @@ typedef struct AfaFwdArgs {
  * the softmax warps' waits for S run out too.  Status word and context as for
  * AFA_TEST_PRODUCER_IDLE. */
 #define AFA_TEST_MMA_IDLE 2u
+/* test_flags bit (causal kernel with scheduler words): the kernel runs normally
+ * but does not return the scheduler words to zero when it ends, so a test can
+ * check that the next call's words are cleared (afa_fwd_sm100_noalloc). */
+#define AFA_TEST_KEEP_SCHED 4u
 
 /*
  * Launch the forward kernel on `stream` (a cudaStream_t) for the current device.
@@ -148,9 +154,11 @@ int afa_fwd_sm100_noalloc(const AfaFwdArgs* args, void* stream);
 const char* afa_strerror(int code);
 
 /*
- * Device status words written by the kernel into AfaFwdArgs.status (first error
- * wins).  AFA_DEV_TIMEOUT_BASE + site: a bounded mbarrier wait at `site` ran
- * out and the kernel returned early (the output is then undefined).
+ * Device status words written by the kernel into AfaFwdArgs.status (plain
+ * stores: when several waits run out, the code of one of them remains; a
+ * non-zero word is never overwritten by a later launch's code unless it is
+ * first reset).  AFA_DEV_TIMEOUT_BASE + site: a bounded mbarrier wait at
+ * `site` ran out and the kernel returned early (the output is then undefined).
  * Decodes a status word into text (static storage).
  */
 #define AFA_DEV_OK 0

@@ -7,8 +7,10 @@ nvcc flags (setup.py:15-51 of the reference) except: PTX only for compute_80
 Ampere kernel on the B200, and no ``--keep`` (no intermediates are written).
 The output is git-ignored and travels to the GPU box as a built file.
 
-Usage: python oracle/build_ref.py [--reference /path/to/reference] [--force]
-Skips (returns None) when the reference tree is absent.
+Usage: python oracle/build_ref.py [--reference DIR] [--force]
+The reference checkout comes from ``--reference`` / the ``reference`` argument,
+else the ``AFA_REFERENCE_DIR`` environment variable; with neither given, or
+when the directory holds no ``csrc/include``, nothing is built (returns None).
 """
 
 from __future__ import annotations
@@ -20,11 +22,21 @@ from pathlib import Path
 
 HERE = Path(__file__).resolve().parent
 OUT = HERE / "_ref" / "libafa_ref_ampere.so"
-DEFAULT_REFERENCE = Path(os.environ.get("AFA_REFERENCE_DIR", "/root/reference"))
 
 
-def build(reference: Path = DEFAULT_REFERENCE, force: bool = False, verbose: bool = False):
-    inc = Path(reference) / "csrc" / "include"
+def reference_dir(reference=None):
+    """The reference checkout to build from: the argument, else $AFA_REFERENCE_DIR; None if neither."""
+    if reference:
+        return Path(reference)
+    env = os.environ.get("AFA_REFERENCE_DIR")
+    return Path(env) if env else None
+
+
+def build(reference=None, force: bool = False, verbose: bool = False):
+    ref = reference_dir(reference)
+    if ref is None:
+        return None
+    inc = ref / "csrc" / "include"
     if not inc.is_dir():
         return None
     src = HERE / "ref_kernel_shim.cu"
@@ -71,7 +83,8 @@ def build(reference: Path = DEFAULT_REFERENCE, force: bool = False, verbose: boo
 
 
 if __name__ == "__main__":
-    ref = DEFAULT_REFERENCE
-    if "--reference" in sys.argv:
-        ref = Path(sys.argv[sys.argv.index("--reference") + 1])
-    print(build(ref, force="--force" in sys.argv, verbose=True))
+    ref = sys.argv[sys.argv.index("--reference") + 1] if "--reference" in sys.argv else None
+    out = build(ref, force="--force" in sys.argv, verbose=True)
+    if out is None:
+        sys.exit("no reference checkout: pass --reference DIR or set AFA_REFERENCE_DIR")
+    print(out)

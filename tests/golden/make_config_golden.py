@@ -6,7 +6,8 @@ lists (string form and C++ struct form), the parse of a set of config strings,
 and is_valid_config over the full tiling grid.  tests/test_config.py compares
 ampere_flash_attention_from_scratch_b200.afa_config with these records.
 
-Usage: python tests/golden/make_config_golden.py [REFERENCE_DIR]
+Usage: python tests/golden/make_config_golden.py REFERENCE_DIR
+(or with AFA_REFERENCE_DIR set in the environment instead of the argument).
 """
 
 import dataclasses
@@ -60,5 +61,10 @@ def main(ref_dir: Path, out: Path):
 
 
 if __name__ == "__main__":
-    ref = Path(sys.argv[1]) if len(sys.argv) > 1 else Path("/root/reference")
+    import os
+
+    arg = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("AFA_REFERENCE_DIR")
+    if not arg:
+        sys.exit("usage: make_config_golden.py REFERENCE_DIR (or set AFA_REFERENCE_DIR)")
+    ref = Path(arg)
     main(ref, Path(__file__).resolve().parent / "config_golden.json")

@@ -56,10 +56,14 @@ def _bench(args, rank):
 def test_reference_arm_rank0_prints_one_line_other_ranks_exit_quietly():
     import json
 
+    import time
+
     args = ["--impl", "reference", "--config", "cfg1", "--gpus", "2", "--steps", "1"]
     r1 = _bench(args, rank=1)
     assert r1.returncode == 0 and r1.stdout.strip() == "", r1.stderr[-2000:]
+    t0 = time.perf_counter()
     r0 = _bench(args, rank=0)
+    wall_ms = (time.perf_counter() - t0) * 1e3
     assert r0.returncode == 0, r0.stderr[-2000:]
     lines = [ln for ln in r0.stdout.splitlines() if ln.strip()]
     assert len(lines) == 1
@@ -70,6 +74,24 @@ def test_reference_arm_rank0_prints_one_line_other_ranks_exit_quietly():
     assert line["e2e"] == {"value": line["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0,
                            "d2h_bytes_per_step": 0}
     assert line["config"]["workload"] == "cfg1"
+    # The line reports the step it ran: its timed steps fit inside the process's wall time.
+    assert line["ms_per_step"] * line["steps"] <= wall_ms
+    assert line["workload_ms_extrapolated"] >= line["ms_per_step"]
+
+
+def test_reference_arm_steps_fit_the_run_at_the_headline_size():
+    """cfg4: one [8192 x 128] slice per step; 512 slices would take ~40 s per step,
+    so a line that multiplied by the slice count would not fit the run."""
+    import json
+    import time
+
+    t0 = time.perf_counter()
+    r = _bench(["--impl", "reference", "--config", "cfg4", "--steps", "2", "--warmup", "3"], rank=0)
+    wall_ms = (time.perf_counter() - t0) * 1e3
+    assert r.returncode == 0, r.stderr[-2000:]
+    line = json.loads(r.stdout.strip().splitlines()[-1])
+    assert line["steps"] == 2 and line["ms_per_step"] * line["steps"] <= wall_ms
+    assert line["workload_ms_extrapolated"] == line["ms_per_step"] * 512
 
 
 def test_reference_arm_has_no_causal_mask():

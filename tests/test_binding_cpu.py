@@ -63,6 +63,14 @@ def test_forward_host_rejects_before_any_cuda_call(args, match):
         fa.forward_host(*args)
 
 
+def test_forward_host_requires_a_page_locked_output():
+    """A copy into pageable memory returns only when it has finished, which would
+    serialise the slices' copies behind the kernels: such an `o` is refused."""
+    q = _h(1, 64, 2, 64)
+    with pytest.raises(RuntimeError, match="o must be page-locked"):
+        fa.forward_host(q, q, q, _h(1, 64, 2, 64))
+
+
 def test_forward_host_rejects_a_mismatched_output():
     q = _h(1, 64, 2, 64)
     with pytest.raises(RuntimeError, match="o must be a contiguous host tensor"):

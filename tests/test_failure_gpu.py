@@ -8,6 +8,10 @@ context must still produce the right answer.  With AFA_TEST_MMA_IDLE the MMA
 issuer issues nothing: the producer fills the K/V ring, its wait for a free
 slot runs out with its loads in flight or landed, and it waits for them before
 the CTA exits -- same checks.
+
+Through the torch binding the status word sits in mapped page-locked host
+memory: a launch that aborted is raised by the next call on the device, without
+check_status(), naming the wait site.
 """
 
 import ctypes
@@ -46,4 +50,62 @@ def test_bounded_wait_runs_out_and_context_survives(flag):
     torch.cuda.synchronize()
     assert int(status.item()) == 0
     mx, mean = error_stats(o, attention_fp32(q, k, v))
+    assert mx <= 1e-2 and mean <= 1e-3
+
+
+def _torch_inputs(seed, d=128, dtype=torch.float16):
+    g = torch.Generator().manual_seed(seed)
+    return [torch.randn(2, 384, 2, d, generator=g).to(dtype) for _ in range(3)]
+
+
+@pytest.mark.parametrize("entry", ["forward", "forward_ext"])
+def test_torch_path_raises_on_the_next_call(entry):
+    import afa_flash_attention_kernels as fa
+    from afa_py.afa_config import AFAForwardKernelConfig, DType
+
+    cfg = AFAForwardKernelConfig(dtype=DType.FP16, d_head=128)
+    q, k, v = _torch_inputs(6)
+    qd, kd, vd = (t.cuda() for t in (q, k, v))
+    fa.check_status(0)  # nothing pending from earlier tests
+    fa._set_test_flags(_abi.AFA_TEST_PRODUCER_IDLE, 20_000_000)
+    if entry == "forward":
+        fa.forward(cfg, qd, kd, vd)  # returns at once; the kernel aborts after 20 ms
+    else:
+        fa.forward_ext(qd, kd, vd)
+    torch.cuda.synchronize()  # the aborted launch has finished (no check_status)
+    with pytest.raises(RuntimeError, match=r"earlier launch on cuda:0.*timeout: (MMA|softmax) waiting"):
+        fa.forward_ext(qd, kd, vd)
+    # Raised once: the word was cleared, and the flags applied to one launch only.
+    o, _ = fa.forward_ext(qd, kd, vd)
+    fa.check_status(0)
+    mx, mean = error_stats(o, attention_fp32(q, k, v))
+    assert mx <= 1e-2 and mean <= 1e-3
+
+
+def test_torch_path_benchmark_call_raises_for_its_own_launch():
+    import afa_flash_attention_kernels as fa
+    from afa_py.afa_config import AFAForwardKernelConfig, DType
+
+    q, k, v = (t.cuda() for t in _torch_inputs(8, d=64, dtype=torch.bfloat16))
+    fa.check_status(0)
+    fa._set_test_flags(_abi.AFA_TEST_MMA_IDLE, 20_000_000)
+    with pytest.raises(RuntimeError, match="attention kernel reported: timeout"):
+        fa.forward(AFAForwardKernelConfig(dtype=DType.BF16, d_head=64), q, k, v, None, True)
+    fa.check_status(0)
+
+
+def test_check_status_raises_after_an_abort():
+    import afa_flash_attention_kernels as fa
+
+    q, k, v = (t.cuda() for t in _torch_inputs(9))
+    fa.check_status(0)
+    fa._set_test_flags(_abi.AFA_TEST_PRODUCER_IDLE, 20_000_000)
+    fa.forward_ext(q, k, v, None, True)  # causal kernel, dynamic schedule
+    with pytest.raises(RuntimeError, match="attention kernel reported: timeout"):
+        fa.check_status(0)
+    fa.check_status(0)  # cleared
+    # The scheduler words came back to zero on the abort path: a normal causal call is complete.
+    o, _ = fa.forward_ext(q, k, v, None, True)
+    fa.check_status(0)
+    mx, mean = error_stats(o, attention_fp32(*(t.cpu() for t in (q, k, v)), causal=True))
     assert mx <= 1e-2 and mean <= 1e-3

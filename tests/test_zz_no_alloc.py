@@ -6,9 +6,12 @@ come from a static __device__ array in the library instead of the caller.
 Checked against the existing entry point (afa_fwd_sm100 with caller-owned
 words) on two consecutive calls: results must be bit-identical (tighter than
 the fp16/bf16 tolerances of the other tests), and the static words, which keep
-the previous call's contents, are reused from one call to the next.  The file
-is named to be collected last, so a run that stops at the first failure has
-run every other test first."""
+the previous call's contents, are reused from one call to the next.  A second
+test leaves the static words non-zero on purpose (AFA_TEST_KEEP_SCHED: the
+kernel skips returning them to zero) and checks that the next call clears them
+before its launch -- without that clear every work item would be skipped.  The
+file is named to be collected last, so a run that stops at the first failure
+has run every other test first."""
 
 import ctypes
 
@@ -78,3 +81,34 @@ def test_matches_existing_entry_point_on_two_calls(causal):
         assert torch.equal(outs[0][0], outs[1][0]), f"call {call}: O differs"
         assert torch.equal(outs[0][1], outs[1][1]), f"call {call}: lse differs"
         assert words.tolist() == [0, 0]
+
+
+@pytest.mark.gpu
+def test_next_call_clears_words_left_non_zero():
+    lib = _abi.load()
+    stream = torch.cuda.current_stream().cuda_stream
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    q, k, v = _inputs(2, 1500, 1500, 4, 2, 128, seed=7)
+
+    # The flag works: with caller-owned words the kernel leaves them non-zero.
+    words = torch.zeros(2, dtype=torch.int32, device="cuda")
+    o_ref = torch.empty_like(q)
+    a = _abi.make_args(q, k, v, o_ref, status=status, causal=True, sched=words,
+                       test_flags=_abi.AFA_TEST_KEEP_SCHED)
+    assert lib.afa_fwd_sm100(ctypes.byref(a), stream) == _abi.AFA_OK
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0
+    assert words.tolist() != [0, 0]
+
+    # The same left-over state in the static array, then a normal no-alloc call.
+    o = torch.empty_like(q)
+    a = _abi.make_args(q, k, v, o, status=status, causal=True, test_flags=_abi.AFA_TEST_KEEP_SCHED)
+    assert lib.afa_fwd_sm100_noalloc(ctypes.byref(a), stream) == _abi.AFA_OK
+    torch.cuda.synchronize()
+    assert torch.equal(o, o_ref)
+    o = torch.full_like(q, float("nan"))
+    a = _abi.make_args(q, k, v, o, status=status, causal=True)
+    assert lib.afa_fwd_sm100_noalloc(ctypes.byref(a), stream) == _abi.AFA_OK
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0, lib.afa_status_string(int(status.item()))
+    assert torch.equal(o, o_ref)
