@@ -11,6 +11,7 @@ for host-resident tensors (copies in, compute and copies out overlapped per batc
 
 from ampere_flash_attention_from_scratch_b200.afa_flash_attention_kernels import (  # noqa: F401
     _raise_formatted_error,
+    _set_test_flags,
     check_status,
     forward,
     forward_ext,

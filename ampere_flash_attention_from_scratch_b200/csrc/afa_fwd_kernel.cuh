@@ -67,7 +67,10 @@ struct FwdParams {
   CUtensorMap tm_q;
   CUtensorMap tm_k;
   CUtensorMap tm_v;
-  unsigned seq_inner_mask;  // bit 0: q, bit 1: k, bit 2: v
+  // O for TMA stores (only with the correction warpgroup): box 64 head_dim
+  // elements x 32 rows, SWIZZLE_128B.
+  CUtensorMap tm_o;
+  unsigned seq_inner_mask;  // bit 0: q, bit 1: k, bit 2: v, bit 3: o
   void* o;
   long long o_sb, o_sn, o_sh;  // element strides of O (head_dim stride is 1)
   int seq_len;     // query rows
@@ -102,12 +105,26 @@ enum WaitSite : int {
   kSiteMmaDrain = 10,
   kSiteLoadItem = 11,  // producer waiting for a free slot of the work-item ring
   kSiteReadItem = 12,  // MMA / softmax warps waiting for the next claimed work item
+  kSiteCorrAlpha = 13, // correction warp waiting for a softmax warp's row scale factors
+  kSiteCorrStats = 14, // correction warp waiting for a softmax warp's final row sums
+  kSiteMmaOFree = 15,  // MMA waiting for the previous item's O to be read out
 };
 
 // Compile-time layout of one kernel instance.
+// With AFA_CORRECTION_WG set, a fourth warpgroup (warps 12-15, one per TMEM
+// lane quadrant) takes the correction role off the softmax warpgroups: it
+// rescales O in TMEM when a softmax warp reports a grown row maximum, and runs
+// the epilogue (O * 1/l, staged through shared memory, TMA-stored), so each
+// softmax warpgroup moves on to the next work item as soon as its last P is
+// handed over.
+#ifndef AFA_CORRECTION_WG
+#define AFA_CORRECTION_WG 0
+#endif
+
 template <int kD, bool kBF16, int kStages>
 struct FwdLayout {
   static_assert(kD == 64 || kD == 128, "head_dim must be 64 or 128");
+  static constexpr bool kCorr = AFA_CORRECTION_WG != 0;
   static constexpr int kBM = 128;  // query rows per Q tile (= TMEM lanes)
   static constexpr int kBN = 128;  // key/value rows per K/V tile
   static constexpr int kAtoms = kD / 64;               // 128-byte swizzle atoms along head_dim
@@ -115,7 +132,15 @@ struct FwdLayout {
   static constexpr uint32_t kTileBytes = kAtoms * kAtomBytes;
   static constexpr uint32_t kOffQ = 0;  // Q0, Q1
   static constexpr uint32_t kOffKV = 2 * kTileBytes;
-  static constexpr uint32_t kOffBar = kOffKV + kStages * kTileBytes;
+  // Correction warpgroup only: per warp a 4 KB staging tile of O (32 rows x
+  // 64 head_dim elements, 128-byte swizzled for the TMA store), the softmax
+  // warps' reference maxima before / after the current tile [2][128] and
+  // final (l, m) per row [2 items][2][128].
+  static constexpr uint32_t kStageBytes = 32u * 128u;
+  static constexpr uint32_t kOffStage = kOffKV + kStages * kTileBytes;
+  static constexpr uint32_t kOffAlpha = kOffStage + (kCorr ? 4u * kStageBytes : 0u);
+  static constexpr uint32_t kOffStats = kOffAlpha + (kCorr ? 2u * 128u * 8u : 0u);
+  static constexpr uint32_t kOffBar = kOffStats + (kCorr ? 2u * 2u * 128u * 8u : 0u);
   // mbarrier indices
   // Each Q tile has its own full/empty pair, so the next work item's Q0 loads
   // as soon as the current item's last S0 is issued.
@@ -154,24 +179,45 @@ struct FwdLayout {
   static constexpr int kItemSlots = 4;
   static constexpr int kBarItemFull = kBarMmaDrain + 1;           // [kItemSlots]
   static constexpr int kBarItemEmpty = kBarItemFull + kItemSlots;  // [kItemSlots]
-  static constexpr uint32_t kItemReaders = 1 + 8;                 // MMA warp + softmax warps
-  static constexpr int kNumBars = kBarItemEmpty + kItemSlots;
+  static constexpr uint32_t kItemReaders = 1 + 8 + (kCorr ? 4 : 0);  // MMA, softmax (+ correction) warps
+  // Correction warpgroup only: alpha ready [wg][quadrant], (l, m) ready
+  // [wg][quadrant] (one arrival each), O read out [wg] (one arrival per
+  // correction warp).  P chunk 0's barrier then also waits for the correction
+  // warps (the O rescale precedes the PV that accumulates into O).
+  static constexpr int kBarAlpha = kBarItemEmpty + kItemSlots;
+  static constexpr int kBarStats = kBarAlpha + (kCorr ? 8 : 0);
+  static constexpr int kBarOFree = kBarStats + (kCorr ? 8 : 0);
+  static constexpr int kNumBars = kBarOFree + (kCorr ? 2 : 0);
   static constexpr uint32_t kOffTmemSlot = kOffBar + kNumBars * 8;
   static constexpr uint32_t kOffAbort = kOffTmemSlot + 4;
   static constexpr uint32_t kOffItems = kOffAbort + 4;            // int[kItemSlots]
   static constexpr uint32_t kSmemUsed = kOffItems + 4 * kItemSlots;
   static constexpr uint32_t kSmemBytes = kSmemUsed + 1024;  // slack for 1024-byte alignment
-  static constexpr int kThreads = 384;
+  static constexpr int kThreads = kCorr ? 512 : 384;
   static constexpr int kSoftmaxThreads = 128;
   static constexpr uint32_t kTmemCols = 512;
   static constexpr uint32_t kColO = 256;  // O0 at 256, O1 at 256 + kD
-  // Register split: launched at kLaunchRegs per thread (384 threads, 1 CTA/SM);
-  // the producer warpgroup drops to kProducerRegs, the two softmax warpgroups
-  // rise to kSoftmaxRegs.  128 * (72 + 216 + 216) == 384 * 168.
-  static constexpr int kLaunchRegs = 168;
-  static constexpr int kProducerRegs = 72;
-  static constexpr int kSoftmaxRegs = 216;
-  static_assert(kProducerRegs + 2 * kSoftmaxRegs <= 3 * kLaunchRegs, "register split too large");
+  // Register split: launched at kLaunchRegs per thread (1 CTA/SM); the
+  // producer warpgroup (and the correction warpgroup) drop to kProducerRegs
+  // (kCorrRegs), the two softmax warpgroups rise to kSoftmaxRegs.
+  // 384 threads: 128 * (72 + 216 + 216) == 384 * 168;
+  // 512 threads: 128 * (40 + 208 + 208 + 56) == 512 * 128 (no spills; the
+  // softmax warps spill below 208, the correction warps below 56).
+#ifndef AFA_CORR_SPLIT_PRODUCER
+#define AFA_CORR_SPLIT_PRODUCER 40
+#endif
+#ifndef AFA_CORR_SPLIT_CORR
+#define AFA_CORR_SPLIT_CORR 56
+#endif
+#ifndef AFA_CORR_SPLIT_SOFTMAX
+#define AFA_CORR_SPLIT_SOFTMAX 208
+#endif
+  static constexpr int kLaunchRegs = kCorr ? 128 : 168;
+  static constexpr int kProducerRegs = kCorr ? AFA_CORR_SPLIT_PRODUCER : 72;
+  static constexpr int kCorrRegs = AFA_CORR_SPLIT_CORR;
+  static constexpr int kSoftmaxRegs = kCorr ? AFA_CORR_SPLIT_SOFTMAX : 216;
+  static_assert(kProducerRegs + 2 * kSoftmaxRegs + (kCorr ? kCorrRegs : 0) <= (kThreads / 128) * kLaunchRegs,
+                "register split too large");
   // Share of exp2 evaluations moved from the MUFU unit to the FMA pipe: in
   // every group of 8 consecutive column pairs, kEmuPairs evenly spaced pairs
   // use the polynomial (0 by default: every share measured so far was slower).  At head_dim 128 the MUFU work per K/V tile equals the MMA
@@ -528,6 +574,12 @@ __device__ __forceinline__ void role_mma(const FwdParams& p, uint32_t sbase, uin
   uint32_t pph[2] = {0u, 0u};
   // O_wg (+)= P_wg V: each P chunk is issued as soon as its barrier flips.
   auto pv = [&](int wg, uint32_t v_addr, bool accumulate) -> bool {
+    if constexpr (L::kCorr) {
+      // The first PV of an item overwrites O_wg: the correction warps must
+      // have read out the previous item's O_wg.
+      if (!accumulate && it > 0u && !sy.wait(bar(L::kBarOFree + wg), (it - 1u) & 1u, kSiteMmaOFree))
+        return false;
+    }
 #pragma unroll
     for (int c = 0; c < L::kPChunks; ++c) {
       if (!sy.wait(bar(L::kBarPReady + wg * L::kPChunks + c), pph[wg], wg ? kSiteMmaP1 : kSiteMmaP0))
@@ -613,7 +665,7 @@ __device__ __forceinline__ void role_mma(const FwdParams& p, uint32_t sbase, uin
 // Role: softmax + correction + epilogue (one warpgroup per Q tile)
 // ---------------------------------------------------------------------------
 template <int kD, bool kBF16, int kStages, bool kCausal>
-__device__ __forceinline__ void role_softmax(const FwdParams& p, int wg, uint32_t bar0,
+__device__ __forceinline__ void role_softmax(const FwdParams& p, int wg, uint8_t* smem, uint32_t bar0,
                                              uint32_t tmem, const CtaSync& sy, const WorkQueue<4>& wq) {
   using L = FwdLayout<kD, kBF16, kStages>;
   using T = typename std::conditional<kBF16, __nv_bfloat16, __half>::type;
@@ -670,7 +722,18 @@ __device__ __forceinline__ void role_softmax(const FwdParams& p, int wg, uint32_
       const bool need = m_new > m_ref + 8.0f;
       // alpha rescales the running sum and O from the old reference max.
       const float alpha = need ? ex2_approx(m_ref - m_new) : 1.0f;
-      if (j > 0 && __any_sync(0xffffffffu, need)) {
+      if constexpr (L::kCorr) {
+        // The correction warp of this quadrant rescales O (if any row of the
+        // warp needs it) and then releases P chunk 0 together with this warp.
+        // It gets the reference maximum before and after this tile and forms
+        // the factor itself, so no exponential precedes the hand-over here.
+        if (j > 0) {
+          reinterpret_cast<float2*>(smem + L::kOffAlpha)[wg * 128 + row] =
+              make_float2(m_ref, need ? m_new : m_ref);
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(L::kBarAlpha + wg * 4 + warp_in_wg));
+        }
+      } else if (j > 0 && __any_sync(0xffffffffu, need)) {
         // Conditional rescale of O, before this step's first P chunk is handed
         // over: the previous PV of this tile has completed (it was committed
         // before S(j)) and the next one waits for that chunk, so O is quiescent.
@@ -715,7 +778,14 @@ __device__ __forceinline__ void role_softmax(const FwdParams& p, int wg, uint32_
         tmem_wait_st();
         tc_fence_before_sync();
         __syncwarp();
-        if (lane == 0) mbar_arrive(bar_p0 + 8u * static_cast<uint32_t>(c));
+        if (lane == 0) {
+          // With the correction warpgroup, chunk 0 also counts the correction
+          // warp of this quadrant, which has nothing to do on a first tile.
+          if (L::kCorr && c == 0 && j == 0)
+            mbar_arrive_cnt(bar_p0, 2u);
+          else
+            mbar_arrive(bar_p0 + 8u * static_cast<uint32_t>(c));
+        }
       };
       // Software-pipelined by one chunk: the store of chunk c-1 drains while
       // chunk c is computed.
@@ -734,6 +804,16 @@ __device__ __forceinline__ void role_softmax(const FwdParams& p, int wg, uint32_
       }
       hand_off(L::kPChunks - 1);
       l = l * alpha + ((acc0.x + acc1.x) + (acc0.y + acc1.y));
+    }
+    if constexpr (L::kCorr) {
+      // The correction warpgroup runs the epilogue from these row statistics
+      // (two slots: this warp may finish the next item before they are read).
+      // (Plain stores and loads: the mbarrier arrive / wait around them are
+      // compiler memory barriers with release / acquire semantics.)
+      reinterpret_cast<float2*>(smem + L::kOffStats)[((it & 1u) * 2u + wg) * 128u + row] = make_float2(l, m_ref);
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar(L::kBarStats + wg * 4 + warp_in_wg));
+      continue;
     }
     // Epilogue: O / l, round to the input type, store the row.  A row that
     // saw no key (causal mask) has l = 0 and O = 0: it stores 0, and a
@@ -770,10 +850,137 @@ __device__ __forceinline__ void role_softmax(const FwdParams& p, int wg, uint32_
 }
 
 // ---------------------------------------------------------------------------
+// Role: correction + epilogue (fourth warpgroup, AFA_CORRECTION_WG only)
+// ---------------------------------------------------------------------------
+// Warp q of the warpgroup reaches TMEM lane quadrant q: rows 32q..32q+31 of
+// both Q tiles.  Per K/V tile j > 0 of each Q tile it takes the row scale
+// factors its softmax peer wrote, rescales those O rows in TMEM when any of
+// them changed (the PV of tile j-1 has completed: the peer saw S(j), committed
+// after it) and then arrives on P chunk 0's barrier, so PV(j) follows the
+// rescale.  After an item's final PV it writes O * 1/l (and the log-sum-exp):
+// 64-column pieces are rounded into a 128-byte-swizzled staging tile and
+// written by TMA stores, and O is released to the next item's first PV as
+// soon as it has been read from TMEM.  Events are taken in a fixed order --
+// the tiles' scale factors, then the epilogues of Q tile 0 and 1 -- which the
+// MMA issue order makes deadlock-free.
+// Numerics as the reference: rescale by exp2(m_old - m_new)
+// (csrc/include/afa_softmax.cuh:50-68), final O / l (:109-127).
+template <int kD, bool kBF16, int kStages, bool kCausal>
+__device__ __forceinline__ void role_correction(const FwdParams& p, uint8_t* smem, uint32_t sbase,
+                                                uint32_t bar0, uint32_t tmem, const CtaSync& sy,
+                                                const WorkQueue<4>& wq) {
+  using L = FwdLayout<kD, kBF16, kStages>;
+  auto bar = [&](int i) { return bar0 + 8u * static_cast<uint32_t>(i); };
+  const int quad = static_cast<int>((threadIdx.x >> 5) & 3u);
+  const uint32_t lane = threadIdx.x & 31u;
+  const int row = quad * 32 + static_cast<int>(lane);
+  const uint32_t lane_field = static_cast<uint32_t>(quad * 32) << 16;
+  const float2* alpha_s = reinterpret_cast<const float2*>(smem + L::kOffAlpha);
+  const float2* stats_s = reinterpret_cast<const float2*>(smem + L::kOffStats);
+  const uint32_t stage = sbase + L::kOffStage + static_cast<uint32_t>(quad) * L::kStageBytes;
+  const bool si = (p.seq_inner_mask & 8u) != 0u;
+  // Barrier phases, bit wg for Q tile wg (bit masks, not arrays: indexed by a
+  // loop variable an array would live in local memory).
+  uint32_t aph = 0u, sph = 0u, oph = 0u;
+  bool ok = true;
+  for (uint32_t it = 0; ok; ++it) {
+    const int w = wq.next(it, sy, kSiteReadItem);
+    if (w < 0) break;
+    int qp, h, b;
+    decode_work<kCausal>(p, w, qp, h, b);
+    const int n0 = kv_tiles<kCausal>(p, qp, 0), n1 = kv_tiles<kCausal>(p, qp, 1);
+    for (int j = 1; j < n1 && ok; ++j) {
+#pragma unroll
+      for (int wg = 0; wg < 2; ++wg) {
+        if (wg == 0 && j >= n0) continue;
+        if (!sy.wait(bar(L::kBarAlpha + wg * 4 + quad), (aph >> wg) & 1u, kSiteCorrAlpha)) { ok = false; break; }
+        aph ^= 1u << wg;
+        // The softmax warp's factor exp2(m_old - m_new) when its reference
+        // maximum moved, else 1 (the same instruction on the same operands).
+        const float2 mm = alpha_s[wg * 128 + row];
+        const bool moved = mm.y != mm.x;
+        if (__any_sync(0xffffffffu, moved)) {
+          const float a = moved ? ex2_approx(mm.x - mm.y) : 1.0f;
+          tc_fence_after_sync();
+          const uint32_t tO = tmem + lane_field + L::kColO + static_cast<uint32_t>(wg * kD);
+#pragma unroll 1
+          for (int c = 0; c < kD / 8; ++c) {
+            uint32_t o[8];
+            tmem_ld8_sync(tO + c * 8u, o);
+#pragma unroll
+            for (int e = 0; e < 8; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * a);
+            tmem_st8(tO + c * 8u, o);
+          }
+          tmem_wait_st();
+        }
+        tc_fence_before_sync();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar(L::kBarPReady + wg * L::kPChunks));
+      }
+    }
+    if (!ok) break;
+#pragma unroll 1
+    for (int wg = 0; wg < 2; ++wg) {
+      if (!sy.wait(bar(L::kBarStats + wg * 4 + quad), (sph >> wg) & 1u, kSiteCorrStats)) { ok = false; break; }
+      sph ^= 1u << wg;
+      if (!sy.wait(bar(L::kBarOFinal + wg), (oph >> wg) & 1u, kSiteSoftmaxO)) { ok = false; break; }
+      oph ^= 1u << wg;
+      tc_fence_after_sync();
+      const float2 st = stats_s[((it & 1u) * 2u + wg) * 128u + row];
+      const float l = st.x, m_ref = st.y;
+      const int row0 = qp * 256 + wg * 128 + quad * 32;
+      const int q_row = row0 + static_cast<int>(lane);
+      if (p.lse != nullptr && q_row < p.seq_len) {
+        // ln(sum_j exp(s_j * scale)) = (m_ref + log2(l)) * ln(2), m_ref in log2 units.
+        const float lse = l > 0.f ? (m_ref + log2f(l)) * 0.69314718055994531f : -INFINITY;
+        p.lse[(static_cast<long long>(b) * p.n_heads + h) * p.seq_len + q_row] = lse;
+      }
+      const float inv_l = l > 0.f ? 1.0f / l : 0.f;
+      const uint32_t tO = tmem + lane_field + L::kColO + static_cast<uint32_t>(wg * kD);
+#pragma unroll 1
+      for (int c = 0; c < kD / 64; ++c) {
+        // The staging tile is free once the previous store has read it.
+        if (lane == 0) bulk_wait_group_read<0>();
+        __syncwarp();
+#pragma unroll 1
+        for (uint32_t k = 0; k < 8u; ++k) {  // 8 columns = one 16-byte chunk of the row
+          uint32_t o[8];
+          tmem_ld8_sync(tO + static_cast<uint32_t>(c * 64) + k * 8u, o);
+          uint32_t pk[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e)
+            pk[e] = pack2<kBF16>(__uint_as_float(o[2 * e]) * inv_l, __uint_as_float(o[2 * e + 1]) * inv_l);
+          // 16-byte chunk k of this row goes to chunk position k ^ (row % 8).
+          st_shared_v4(stage + lane * 128u + ((k ^ (lane & 7u)) << 4), pk[0], pk[1], pk[2], pk[3]);
+        }
+        if (c == kD / 64 - 1) {
+          // All of O_wg's rows of this warp have been read: the next item's
+          // first PV may overwrite them.
+          tc_fence_before_sync();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(bar(L::kBarOFree + wg));
+        }
+        fence_proxy_async_shared();
+        __syncwarp();
+        // Rows past seq_len are clipped by the store; a tile wholly past it is skipped.
+        if (lane == 0 && row0 < p.seq_len) {
+          tma_store_4d(&p.tm_o, stage, c * 64, si ? row0 : h, si ? h : row0, b);
+          bulk_commit_group();
+        }
+      }
+    }
+  }
+  // Every store has finished before the CTA (and its shared memory) goes away.
+  if (lane == 0) bulk_wait_group<0>();
+  __syncwarp();
+}
+
+// ---------------------------------------------------------------------------
 // Kernel
 // ---------------------------------------------------------------------------
 template <int kD, bool kBF16, int kStages, bool kCausal>
-__global__ void __launch_bounds__(384, 1) afa_fwd_sm100_kernel(const __grid_constant__ FwdParams p) {
+__global__ void __launch_bounds__(FwdLayout<kD, kBF16, kStages>::kThreads, 1)
+    afa_fwd_sm100_kernel(const __grid_constant__ FwdParams p) {
   using L = FwdLayout<kD, kBF16, kStages>;
   extern __shared__ __align__(1024) uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
@@ -790,7 +997,9 @@ __global__ void __launch_bounds__(384, 1) afa_fwd_sm100_kernel(const __grid_cons
     for (int i = 0; i < L::kNumBars; ++i) {
       // p_ready: one elected arrival per softmax warp; all others: one arrival.
       uint32_t count = 1u;
-      if (i >= L::kBarPReady && i < L::kBarPReady + 2 * L::kPChunks) count = 4u;
+      if (i >= L::kBarPReady && i < L::kBarPReady + 2 * L::kPChunks)
+        count = (L::kCorr && (i - L::kBarPReady) % L::kPChunks == 0) ? 8u : 4u;
+      if (L::kCorr && i >= L::kBarOFree && i < L::kBarOFree + 2) count = 4u;
       if (i >= L::kBarItemEmpty && i < L::kBarItemEmpty + L::kItemSlots) count = L::kItemReaders;
       mbar_init(bar0 + 8u * i, count);
     }
@@ -799,6 +1008,7 @@ __global__ void __launch_bounds__(384, 1) afa_fwd_sm100_kernel(const __grid_cons
     tma_prefetch_desc(&p.tm_q);
     tma_prefetch_desc(&p.tm_k);
     tma_prefetch_desc(&p.tm_v);
+    if (L::kCorr) tma_prefetch_desc(&p.tm_o);
   }
   if (warp == 2) {
     tmem_alloc(smem_u32(tmem_slot), L::kTmemCols);
@@ -823,9 +1033,14 @@ __global__ void __launch_bounds__(384, 1) afa_fwd_sm100_kernel(const __grid_cons
     } else if (warp == 1) {
       role_mma<kD, kBF16, kStages, kCausal>(p, sbase, bar0, tmem, sy, wq);
     }
-  } else {
+  } else if (warp < 12) {
     setmaxnreg_inc<L::kSoftmaxRegs>();
-    role_softmax<kD, kBF16, kStages, kCausal>(p, (warp - 4) >> 2, bar0, tmem, sy, wq);
+    role_softmax<kD, kBF16, kStages, kCausal>(p, (warp - 4) >> 2, smem, bar0, tmem, sy, wq);
+  } else {
+    if constexpr (L::kCorr) {
+      setmaxnreg_dec<L::kCorrRegs>();
+      role_correction<kD, kBF16, kStages, kCausal>(p, smem, sbase, bar0, tmem, sy, wq);
+    }
   }
 
   tc_fence_before_sync();

@@ -73,7 +73,7 @@ def test_torch_path_raises_on_the_next_call(entry):
     else:
         fa.forward_ext(qd, kd, vd)
     torch.cuda.synchronize()  # the aborted launch has finished (no check_status)
-    with pytest.raises(RuntimeError, match=r"earlier launch on cuda:0.*timeout: (MMA|softmax) waiting"):
+    with pytest.raises(RuntimeError, match=r"earlier launch on cuda:0.*timeout: .*waiting"):
         fa.forward_ext(qd, kd, vd)
     # Raised once: the word was cleared, and the flags applied to one launch only.
     o, _ = fa.forward_ext(qd, kd, vd)
