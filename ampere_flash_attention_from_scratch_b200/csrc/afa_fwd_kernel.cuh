@@ -162,10 +162,16 @@ struct FwdLayout {
   // Chunk c covers S columns [chunk_begin(c), chunk_begin(c + 1)).  With two
   // chunks the split may be uneven (kPSplit): a short last chunk shortens the
   // PV that stands between the last hand-off and the next S on the critical path.
+  // At head_dim 64 the PV MMAs (N = 64) are issue-bound (~48 cycles each for
+  // 32 cycles of work), so a 32-column last chunk (2 MMAs instead of 4) pays
+  // there; at 128 the even split is as fast.
 #ifndef AFA_P_SPLIT
 #define AFA_P_SPLIT 64
 #endif
-  static constexpr int kPSplit = AFA_P_SPLIT;
+#ifndef AFA_P_SPLIT_D64
+#define AFA_P_SPLIT_D64 96
+#endif
+  static constexpr int kPSplit = kD == 64 ? AFA_P_SPLIT_D64 : AFA_P_SPLIT;
   static_assert(kPChunks != 2 || (kPSplit % 32 == 0 && kPSplit > 0 && kPSplit < kBN),
                 "the chunk split must fall on a 32-column boundary (16 packed P columns)");
   __host__ __device__ static constexpr int chunk_begin(int c) {
