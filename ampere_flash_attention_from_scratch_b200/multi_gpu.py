@@ -11,6 +11,7 @@ measurements and works with the NCCL (GPU) and gloo (CPU tests) backends.
 
 from __future__ import annotations
 
+import contextlib
 import os
 from dataclasses import dataclass
 from datetime import timedelta
@@ -97,3 +98,39 @@ def gather_to_rank0(local: torch.Tensor, device=None):
 def destroy() -> None:
     if dist.is_initialized():
         dist.destroy_process_group()
+
+
+def gpu_local_cpus(device_index: int):
+    """The CPU cores NVML reports as local to CUDA device `device_index` (its
+    NUMA node), restricted to the cores this process may run on; None when
+    NVML or the device cannot say.  Reads only; changes no GPU setting."""
+    try:
+        import pynvml
+
+        pynvml.nvmlInit()
+        props = torch.cuda.get_device_properties(device_index)
+        bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+        handle = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+        words = pynvml.nvmlDeviceGetCpuAffinity(handle, ((os.cpu_count() or 1) + 63) // 64)
+        cpus = {w * 64 + b for w, mask in enumerate(words) for b in range(64) if (mask >> b) & 1}
+        cpus &= os.sched_getaffinity(0)
+        return cpus or None
+    except Exception:
+        return None
+
+
+@contextlib.contextmanager
+def numa_local(device_index: int):
+    """Runs the body with this process bound to the cores local to GPU
+    `device_index`, so page-locked host buffers allocated inside land on the
+    GPU's NUMA node (copies then do not cross the inter-socket link); the
+    previous affinity is restored afterwards.  A no-op where the local cores
+    are unknown."""
+    before = os.sched_getaffinity(0)
+    cpus = gpu_local_cpus(device_index)
+    if cpus:
+        os.sched_setaffinity(0, cpus)
+    try:
+        yield cpus
+    finally:
+        os.sched_setaffinity(0, before)

@@ -109,3 +109,17 @@ def test_rank_leaving_is_detected():
     res = _run("leave")
     kinds = sorted(r[0] for r in res)
     assert kinds == ["error", "left"], res
+
+
+def test_numa_local_restores_affinity_and_is_a_no_op_without_nvml_device():
+    """numa_local() binds only where NVML names the GPU's cores (not on this CPU
+    machine) and always restores the process's affinity afterwards."""
+    import os
+
+    from ampere_flash_attention_from_scratch_b200 import multi_gpu
+
+    before = os.sched_getaffinity(0)
+    assert multi_gpu.gpu_local_cpus(0) is None
+    with multi_gpu.numa_local(0) as cpus:
+        assert cpus is None and os.sched_getaffinity(0) == before
+    assert os.sched_getaffinity(0) == before
