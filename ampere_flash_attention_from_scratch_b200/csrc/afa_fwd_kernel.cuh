@@ -67,8 +67,8 @@ struct FwdParams {
   CUtensorMap tm_q;
   CUtensorMap tm_k;
   CUtensorMap tm_v;
-  // O for TMA stores (only with the correction warpgroup): box 64 head_dim
-  // elements x 32 rows, SWIZZLE_128B.
+  // O for TMA stores (correction warpgroup, or AFA_O_TMA_STORE): box 64
+  // head_dim elements x 32 rows, SWIZZLE_128B.
   CUtensorMap tm_o;
   unsigned seq_inner_mask;  // bit 0: q, bit 1: k, bit 2: v, bit 3: o
   void* o;
@@ -120,11 +120,18 @@ enum WaitSite : int {
 #ifndef AFA_CORRECTION_WG
 #define AFA_CORRECTION_WG 0
 #endif
+#ifndef AFA_O_TMA_STORE
+#define AFA_O_TMA_STORE 1
+#endif
 
 template <int kD, bool kBF16, int kStages>
 struct FwdLayout {
   static_assert(kD == 64 || kD == 128, "head_dim must be 64 or 128");
   static constexpr bool kCorr = AFA_CORRECTION_WG != 0;
+  // The softmax warps' epilogue writes O through a swizzled shared-memory tile
+  // and TMA stores (whole 128-byte lines) instead of one 16-byte store per row
+  // and lane.
+  static constexpr bool kOTma = AFA_O_TMA_STORE != 0 && !kCorr;
   static constexpr int kBM = 128;  // query rows per Q tile (= TMEM lanes)
   static constexpr int kBN = 128;  // key/value rows per K/V tile
   static constexpr int kAtoms = kD / 64;               // 128-byte swizzle atoms along head_dim
@@ -138,7 +145,8 @@ struct FwdLayout {
   // final (l, m) per row [2 items][2][128].
   static constexpr uint32_t kStageBytes = 32u * 128u;
   static constexpr uint32_t kOffStage = kOffKV + kStages * kTileBytes;
-  static constexpr uint32_t kOffAlpha = kOffStage + (kCorr ? 4u * kStageBytes : 0u);
+  static constexpr uint32_t kStageTiles = kCorr ? 4u : (kOTma ? 8u : 0u);  // one per epilogue warp
+  static constexpr uint32_t kOffAlpha = kOffStage + kStageTiles * kStageBytes;
   static constexpr uint32_t kOffStats = kOffAlpha + (kCorr ? 2u * 128u * 8u : 0u);
   static constexpr uint32_t kOffBar = kOffStats + (kCorr ? 2u * 2u * 128u * 8u : 0u);
   // mbarrier indices
@@ -834,6 +842,44 @@ __device__ __forceinline__ void role_softmax(const FwdParams& p, int wg, uint8_t
       const float lse = l > 0.f ? (m_ref + log2f(l)) * 0.69314718055994531f : -INFINITY;
       p.lse[(static_cast<long long>(b) * p.n_heads + h) * p.seq_len + q_row] = lse;
     }
+    if constexpr (L::kOTma) {
+      // 64-column pieces of this warp's 32 rows go to its staging tile (16-byte
+      // chunk k of a row at chunk position k ^ (row % 8), the 128-byte swizzle
+      // of the O tensor map) and out with one TMA store each; rows past
+      // seq_len are clipped by the store.
+      const uint32_t stage = smem_u32(smem) + L::kOffStage +
+                             static_cast<uint32_t>(wg * 4 + warp_in_wg) * L::kStageBytes;
+      const int row0 = qp * 256 + wg * 128 + warp_in_wg * 32;
+      const bool si = (p.seq_inner_mask & 8u) != 0u;
+#pragma unroll
+      for (int c = 0; c < kD / 64; ++c) {
+        if (lane == 0) bulk_wait_group_read<0>();  // the previous store has read the tile
+        __syncwarp();
+#pragma unroll
+        for (int hh = 0; hh < 2; ++hh) {
+          uint32_t o[32];
+          tmem_ld32_sync(tO + static_cast<uint32_t>(c * 64 + hh * 32), o);
+#pragma unroll
+          for (int q4 = 0; q4 < 4; ++q4) {
+            uint32_t pk[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              pk[e] = pack2<kBF16>(__uint_as_float(o[8 * q4 + 2 * e]) * inv_l,
+                                   __uint_as_float(o[8 * q4 + 2 * e + 1]) * inv_l);
+            const uint32_t k = static_cast<uint32_t>(hh * 4 + q4);
+            st_shared_v4(stage + lane * 128u + ((k ^ (lane & 7u)) << 4), pk[0], pk[1], pk[2], pk[3]);
+          }
+        }
+        fence_proxy_async_shared();
+        __syncwarp();
+        if (lane == 0 && row0 < p.seq_len) {
+          tma_store_4d(&p.tm_o, stage, c * 64, si ? row0 : h, si ? h : row0, b);
+          bulk_commit_group();
+        }
+      }
+      tc_fence_before_sync();
+      continue;
+    }
     T* orow = static_cast<T*>(p.o) + static_cast<long long>(b) * p.o_sb +
               static_cast<long long>(q_row) * p.o_sn + static_cast<long long>(h) * p.o_sh;
 #pragma unroll
@@ -1014,7 +1060,7 @@ __global__ void __launch_bounds__(FwdLayout<kD, kBF16, kStages>::kThreads, 1)
     tma_prefetch_desc(&p.tm_q);
     tma_prefetch_desc(&p.tm_k);
     tma_prefetch_desc(&p.tm_v);
-    if (L::kCorr) tma_prefetch_desc(&p.tm_o);
+    if (L::kCorr || L::kOTma) tma_prefetch_desc(&p.tm_o);
   }
   if (warp == 2) {
     tmem_alloc(smem_u32(tmem_slot), L::kTmemCols);
@@ -1042,6 +1088,8 @@ __global__ void __launch_bounds__(FwdLayout<kD, kBF16, kStages>::kThreads, 1)
   } else if (warp < 12) {
     setmaxnreg_inc<L::kSoftmaxRegs>();
     role_softmax<kD, kBF16, kStages, kCausal>(p, (warp - 4) >> 2, smem, bar0, tmem, sy, wq);
+    // Every TMA store of O has finished before the CTA (and its shared memory) goes away.
+    if (L::kOTma && lane == 0) bulk_wait_group<0>();
   } else {
     if constexpr (L::kCorr) {
       setmaxnreg_dec<L::kCorrRegs>();
