@@ -546,13 +546,19 @@ __device__ __forceinline__ void issue_qk(uint32_t d_tmem, uint32_t q_addr, uint3
                                          uint32_t issue) {
   using L = FwdLayout<kD, kBF16, kStages>;
   constexpr uint32_t kIdesc = idesc_f16_f32(128, 128, kBF16, false);
+  const uint32_t q_lo = sdesc_lo(q_addr, 16), k_lo = sdesc_lo(k_addr, 16);
 #pragma unroll
   for (int k = 0; k < kD / 16; ++k) {
     // K-major SW128: 16-element (32-byte) steps inside a 64-element atom,
     // then the next atom (next TMA box) for head_dim >= 64.
     const uint32_t off = (k / 4) * L::kAtomBytes + (k % 4) * 32u;
-    umma_f16_ss(d_tmem, sdesc_lo(q_addr + off, 16), sdesc_lo(k_addr + off, 16), kIdesc,
-                k > 0 ? 1u : 0u, issue);
+    // The 14-bit address field of the base descriptor plus the step in 16-byte
+    // units: shared-memory addresses stay below 2^18 bytes, so nothing carries
+    // out of the field and the result equals sdesc_lo(addr + off) -- one add
+    // per operand instead of a full descriptor computation per K step (fewer
+    // instructions on the MMA warp's sub-partition, which it shares with two
+    // softmax warps).
+    umma_f16_ss(d_tmem, q_lo + (off >> 4), k_lo + (off >> 4), kIdesc, k > 0 ? 1u : 0u, issue);
   }
 }
 
@@ -562,13 +568,14 @@ __device__ __forceinline__ void issue_pv_chunk(uint32_t d_tmem, uint32_t p_tmem,
                                                int chunk, bool accumulate, uint32_t issue) {
   using L = FwdLayout<kD, kBF16, kStages>;
   constexpr uint32_t kIdesc = idesc_f16_f32(128, kD, kBF16, true);
+  const uint32_t v_lo = sdesc_lo(v_addr, L::kAtomBytes);
 #pragma unroll
   for (int k = L::chunk_begin(chunk) / 16; k < L::chunk_begin(chunk + 1) / 16; ++k) {
     const int i = k - L::chunk_begin(chunk) / 16;
     // V is MN-major (head_dim contiguous): 8-row groups 1024 B apart (SBO),
     // 64-element head_dim atoms one TMA box apart (LBO); 16 key rows per step.
     // P in TMEM: 16 elements of 16 bit = 8 columns per K step.
-    umma_f16_ts(d_tmem, p_tmem + k * 8u, sdesc_lo(v_addr + k * 16u * 128u, L::kAtomBytes), kIdesc,
+    umma_f16_ts(d_tmem, p_tmem + k * 8u, v_lo + static_cast<uint32_t>(k) * (16u * 128u >> 4), kIdesc,
                 (accumulate || i > 0) ? 1u : 0u, issue);
   }
 }
