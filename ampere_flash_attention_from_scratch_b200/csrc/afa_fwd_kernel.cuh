@@ -612,6 +612,15 @@ __device__ __forceinline__ void role_mma(const FwdParams& p, uint32_t sbase, uin
     return true;
   };
   bool ok = (p.test_flags & 2u) == 0u;  // bit 1: issue nothing; the other roles' waits run out
+  // Without the causal mask (static schedule) the next work item's first S0
+  // is issued between the current item's last PV0 and PV1, so Q tile 0's
+  // warpgroup finds it ready after its epilogue instead of after Q tile 1's
+  // last softmax and PV (the item boundary of short sequences).
+#ifndef AFA_EAGER_S0
+#define AFA_EAGER_S0 1
+#endif
+  constexpr bool kEagerS0 = !kCausal && AFA_EAGER_S0 != 0;
+  bool s0_early = false;  // this item's S0(0) was issued during the previous item
   for (; ok; ++it) {
     const int w = wq.next(it, sy, kSiteReadItem);
     if (w < 0) break;  // done, or aborted
@@ -625,13 +634,16 @@ __device__ __forceinline__ void role_mma(const FwdParams& p, uint32_t sbase, uin
       n0 = kv_tiles<kCausal>(p, qp, 0);
       n1 = kv_tiles<kCausal>(p, qp, 1);
     }
-    if (!sy.wait(bar(L::kBarQFull + 0), it & 1u, kSiteMmaQFull)) { ok = false; break; }
     uint32_t ks = kv_cnt % kStages;
-    if (!sy.wait(bar(L::kBarKVFull + ks), (kv_cnt / kStages) & 1u, kSiteMmaKFull)) { ok = false; break; }
-    tc_fence_after_sync();
-    issue_qk<kD, kBF16, kStages>(tS[0], qa[0], slot_addr(ks), leader);
-    umma_commit(bar(L::kBarSFull + 0), leader);
-    if (n0 == 1) umma_commit(bar(L::kBarQEmpty + 0), leader);  // last S0 of the item issued
+    if (!s0_early) {
+      if (!sy.wait(bar(L::kBarQFull + 0), it & 1u, kSiteMmaQFull)) { ok = false; break; }
+      if (!sy.wait(bar(L::kBarKVFull + ks), (kv_cnt / kStages) & 1u, kSiteMmaKFull)) { ok = false; break; }
+      tc_fence_after_sync();
+      issue_qk<kD, kBF16, kStages>(tS[0], qa[0], slot_addr(ks), leader);
+      umma_commit(bar(L::kBarSFull + 0), leader);
+      if (n0 == 1) umma_commit(bar(L::kBarQEmpty + 0), leader);  // last S0 of the item issued
+    }
+    s0_early = false;
     if (!sy.wait(bar(L::kBarQFull + 1), it & 1u, kSiteMmaQFull)) { ok = false; break; }
     tc_fence_after_sync();
     issue_qk<kD, kBF16, kStages>(tS[1], qa[1], slot_addr(ks), leader);
@@ -671,6 +683,20 @@ __device__ __forceinline__ void role_mma(const FwdParams& p, uint32_t sbase, uin
     if (n0 == n1) {
       if (!pv(0, slot_addr(vs), n1 > 1)) { ok = false; break; }
       umma_commit(bar(L::kBarOFinal + 0), leader);
+      if constexpr (kEagerS0) {
+        // The next item (static schedule: the same arithmetic as every role's
+        // next call) and its K_0, whose ring slot is not the one V is in.
+        if (wq.next(it + 1u, sy, kSiteReadItem) >= 0) {
+          const uint32_t kn = kv_cnt % kStages;
+          if (!sy.wait(bar(L::kBarQFull + 0), (it + 1u) & 1u, kSiteMmaQFull)) { ok = false; break; }
+          if (!sy.wait(bar(L::kBarKVFull + kn), (kv_cnt / kStages) & 1u, kSiteMmaKFull)) { ok = false; break; }
+          tc_fence_after_sync();
+          issue_qk<kD, kBF16, kStages>(tS[0], qa[0], slot_addr(kn), leader);
+          umma_commit(bar(L::kBarSFull + 0), leader);
+          if (p.n_kv == 1) umma_commit(bar(L::kBarQEmpty + 0), leader);
+          s0_early = true;
+        }
+      }
     }
     if (!pv(1, slot_addr(vs), n1 > 1)) { ok = false; break; }
     umma_commit(bar(L::kBarOFinal + 1), leader);
