@@ -612,17 +612,26 @@ __device__ __forceinline__ void role_mma(const FwdParams& p, uint32_t sbase, uin
     return true;
   };
   bool ok = (p.test_flags & 2u) == 0u;  // bit 1: issue nothing; the other roles' waits run out
-  // Without the causal mask (static schedule) the next work item's first S0
-  // is issued between the current item's last PV0 and PV1, so Q tile 0's
-  // warpgroup finds it ready after its epilogue instead of after Q tile 1's
-  // last softmax and PV (the item boundary of short sequences).
+  // The next work item's first S0 is issued before the current item's last
+  // PV1 (after its last PV0), so Q tile 0's warpgroup finds it ready after
+  // its epilogue instead of after Q tile 1's last softmax and PV (the item
+  // boundary of short sequences).  Its K_0 can load by then: of the ring only
+  // the last V is still held.  Not in the causal kernel at head_dim 128,
+  // where it measured 0.2-0.5 % slower (+0.8-3.3 % at head_dim 64).
 #ifndef AFA_EAGER_S0
 #define AFA_EAGER_S0 1
 #endif
-  constexpr bool kEagerS0 = !kCausal && AFA_EAGER_S0 != 0;
-  bool s0_early = false;  // this item's S0(0) was issued during the previous item
+#ifndef AFA_EAGER_S0_CAUSAL_D128
+#define AFA_EAGER_S0_CAUSAL_D128 0
+#endif
+  constexpr bool kEagerS0 =
+      AFA_EAGER_S0 != 0 && (!kCausal || kD == 64 || AFA_EAGER_S0_CAUSAL_D128 != 0);
+  bool s0_early = false;   // this item's S0(0) was issued during the previous item
+  bool have_next = false;  // the next item was read from the queue already
+  int w_next = 0;
   for (; ok; ++it) {
-    const int w = wq.next(it, sy, kSiteReadItem);
+    const int w = have_next ? w_next : wq.next(it, sy, kSiteReadItem);
+    have_next = false;
     if (w < 0) break;  // done, or aborted
     // Q tile 0 visits n0 K/V tiles, Q tile 1 n1 >= n0 (equal without a causal
     // mask; the work item is only decoded when they can differ, since this
@@ -683,19 +692,27 @@ __device__ __forceinline__ void role_mma(const FwdParams& p, uint32_t sbase, uin
     if (n0 == n1) {
       if (!pv(0, slot_addr(vs), n1 > 1)) { ok = false; break; }
       umma_commit(bar(L::kBarOFinal + 0), leader);
-      if constexpr (kEagerS0) {
-        // The next item (static schedule: the same arithmetic as every role's
-        // next call) and its K_0, whose ring slot is not the one V is in.
-        if (wq.next(it + 1u, sy, kSiteReadItem) >= 0) {
-          const uint32_t kn = kv_cnt % kStages;
-          if (!sy.wait(bar(L::kBarQFull + 0), (it + 1u) & 1u, kSiteMmaQFull)) { ok = false; break; }
-          if (!sy.wait(bar(L::kBarKVFull + kn), (kv_cnt / kStages) & 1u, kSiteMmaKFull)) { ok = false; break; }
-          tc_fence_after_sync();
-          issue_qk<kD, kBF16, kStages>(tS[0], qa[0], slot_addr(kn), leader);
-          umma_commit(bar(L::kBarSFull + 0), leader);
-          if (p.n_kv == 1) umma_commit(bar(L::kBarQEmpty + 0), leader);
-          s0_early = true;
+    }
+    if constexpr (kEagerS0) {
+      // The next item (read once; the next iteration takes it from here) and
+      // its K_0, whose ring slot is not the one V is in.
+      w_next = wq.next(it + 1u, sy, kSiteReadItem);
+      have_next = true;
+      if (w_next >= 0) {
+        int n0n = p.n_kv;
+        if (kCausal) {
+          int qp, h, b;
+          decode_work<kCausal>(p, w_next, qp, h, b);
+          n0n = kv_tiles<kCausal>(p, qp, 0);
         }
+        const uint32_t kn = kv_cnt % kStages;
+        if (!sy.wait(bar(L::kBarQFull + 0), (it + 1u) & 1u, kSiteMmaQFull)) { ok = false; break; }
+        if (!sy.wait(bar(L::kBarKVFull + kn), (kv_cnt / kStages) & 1u, kSiteMmaKFull)) { ok = false; break; }
+        tc_fence_after_sync();
+        issue_qk<kD, kBF16, kStages>(tS[0], qa[0], slot_addr(kn), leader);
+        umma_commit(bar(L::kBarSFull + 0), leader);
+        if (n0n == 1) umma_commit(bar(L::kBarQEmpty + 0), leader);
+        s0_early = true;
       }
     }
     if (!pv(1, slot_addr(vs), n1 > 1)) { ok = false; break; }
