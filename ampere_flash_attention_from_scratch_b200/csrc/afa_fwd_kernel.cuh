@@ -749,13 +749,16 @@ __device__ __forceinline__ void role_softmax(const FwdParams& p, int wg, uint8_t
   for (uint32_t it = 0;; ++it) {
     const int w = wq.next(it, sy, kSiteReadItem);
     if (w < 0) return;  // done, or aborted
-    int qp, h, b;
-    decode_work<kCausal>(p, w, qp, h, b);
-    const int q_row = qp * 256 + wg * 128 + row;
+    // The item's coordinates (integer divisions): needed up front only under
+    // the causal mask; otherwise decoded while the final O is awaited, off
+    // the item boundary.
+    int qp = 0, h = 0, b = 0;
+    if constexpr (kCausal) decode_work<kCausal>(p, w, qp, h, b);
     const int n_tiles = kv_tiles<kCausal>(p, qp, wg);
     // Keys this row sees: all seq_len_kv, or under the causal mask those with
     // index <= q_row + causal_off.
-    const int row_keys = kCausal ? min(q_row + p.causal_off + 1, p.seq_len_kv) : p.seq_len_kv;
+    const int row_keys =
+        kCausal ? min(qp * 256 + wg * 128 + row + p.causal_off + 1, p.seq_len_kv) : p.seq_len_kv;
     float m_ref = -INFINITY;  // running reference max, already in log2 units (x scale*log2e)
     float l = 0.f;
     for (int j = 0; j < n_tiles; ++j) {
@@ -882,6 +885,8 @@ __device__ __forceinline__ void role_softmax(const FwdParams& p, int wg, uint8_t
     // Epilogue: O / l, round to the input type, store the row.  A row that
     // saw no key (causal mask) has l = 0 and O = 0: it stores 0, and a
     // log-sum-exp of -inf.
+    if constexpr (!kCausal) decode_work<kCausal>(p, w, qp, h, b);
+    const int q_row = qp * 256 + wg * 128 + row;
     if (!sy.wait(bar_o, oph, kSiteSoftmaxO)) return;
     oph ^= 1u;
     tc_fence_after_sync();
@@ -901,31 +906,35 @@ __device__ __forceinline__ void role_softmax(const FwdParams& p, int wg, uint8_t
                              static_cast<uint32_t>(wg * 4 + warp_in_wg) * L::kStageBytes;
       const int row0 = qp * 256 + wg * 128 + warp_in_wg * 32;
       const bool si = (p.seq_inner_mask & 8u) != 0u;
-#pragma unroll
-      for (int c = 0; c < kD / 64; ++c) {
-        if (lane == 0) bulk_wait_group_read<0>();  // the previous store has read the tile
-        __syncwarp();
+      // Piece c + 1 is read from TMEM and rounded while piece c's store is
+      // still reading the staging tile.
+      uint32_t pc[32];
+      auto load_piece = [&](int c) {
 #pragma unroll
         for (int hh = 0; hh < 2; ++hh) {
           uint32_t o[32];
           tmem_ld32_sync(tO + static_cast<uint32_t>(c * 64 + hh * 32), o);
 #pragma unroll
-          for (int q4 = 0; q4 < 4; ++q4) {
-            uint32_t pk[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-              pk[e] = pack2<kBF16>(__uint_as_float(o[8 * q4 + 2 * e]) * inv_l,
-                                   __uint_as_float(o[8 * q4 + 2 * e + 1]) * inv_l);
-            const uint32_t k = static_cast<uint32_t>(hh * 4 + q4);
-            st_shared_v4(stage + lane * 128u + ((k ^ (lane & 7u)) << 4), pk[0], pk[1], pk[2], pk[3]);
-          }
+          for (int e = 0; e < 16; ++e)
+            pc[hh * 16 + e] = pack2<kBF16>(__uint_as_float(o[2 * e]) * inv_l, __uint_as_float(o[2 * e + 1]) * inv_l);
         }
+      };
+      load_piece(0);
+#pragma unroll
+      for (int c = 0; c < kD / 64; ++c) {
+        if (lane == 0) bulk_wait_group_read<0>();  // the previous store has read the tile
+        __syncwarp();
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          st_shared_v4(stage + lane * 128u + ((static_cast<uint32_t>(k) ^ (lane & 7u)) << 4), pc[4 * k],
+                       pc[4 * k + 1], pc[4 * k + 2], pc[4 * k + 3]);
         fence_proxy_async_shared();
         __syncwarp();
         if (lane == 0 && row0 < p.seq_len) {
           tma_store_4d(&p.tm_o, stage, c * 64, si ? row0 : h, si ? h : row0, b);
           bulk_commit_group();
         }
+        if (c + 1 < kD / 64) load_piece(c + 1);
       }
       tc_fence_before_sync();
       continue;
