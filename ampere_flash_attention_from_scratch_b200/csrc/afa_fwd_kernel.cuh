@@ -483,44 +483,44 @@ __device__ __forceinline__ void role_load(const FwdParams& p, uint32_t sbase, ui
       ok = load_kv(0, 0) && load_q(0) && load_kv(0, 1) && load_q(1);
       for (int j = 1; j < n_tiles && ok; ++j) ok = load_kv(j, 0) && load_kv(j, 1);
       if (!ok) break;
-      continue;
-    }
+    } else {
 #pragma unroll
-    for (int t = 0; t < 2; ++t) {
-      if (!sy.wait(bar(L::kBarQEmpty + t), (it & 1u) ^ 1u, kSiteLoadQEmpty)) { ok = false; break; }
-      if (leader) mbar_arrive_expect_tx(bar(L::kBarQFull + t), L::kTileBytes);
-#pragma unroll
-      for (int a = 0; a < L::kAtoms; ++a) {
-        const int row0 = qp * 256 + t * 128;
-        const bool si = (p.seq_inner_mask & 1u) != 0u;
-        if (leader)
-          tma_load_4d(sbase + L::kOffQ + t * L::kTileBytes + a * L::kAtomBytes, &p.tm_q,
-                      bar(L::kBarQFull + t), a * 64, si ? row0 : h, si ? h : row0, b, pol_q);
-      }
-      ++q_cnt[t];
-    }
-    if (!ok) break;
-    for (int j = 0; j < n_tiles && ok; ++j) {
-#pragma unroll
-      for (int kv = 0; kv < 2; ++kv) {
-        const uint32_t slot = kv_cnt % kStages;
-        const uint32_t ph = (kv_cnt / kStages) & 1u;
-        if (!sy.wait(bar(L::kBarKVEmpty + slot), ph ^ 1u, kSiteLoadKVEmpty)) { ok = false; break; }
-        if (leader) mbar_arrive_expect_tx(bar(L::kBarKVFull + slot), L::kTileBytes);
-        const CUtensorMap* map = kv ? &p.tm_v : &p.tm_k;
-        const bool si = (p.seq_inner_mask & (kv ? 4u : 2u)) != 0u;
-        const int row0 = j * 128;
+      for (int t = 0; t < 2; ++t) {
+        if (!sy.wait(bar(L::kBarQEmpty + t), (it & 1u) ^ 1u, kSiteLoadQEmpty)) { ok = false; break; }
+        if (leader) mbar_arrive_expect_tx(bar(L::kBarQFull + t), L::kTileBytes);
 #pragma unroll
         for (int a = 0; a < L::kAtoms; ++a) {
+          const int row0 = qp * 256 + t * 128;
+          const bool si = (p.seq_inner_mask & 1u) != 0u;
           if (leader)
-            tma_load_4d(sbase + L::kOffKV + slot * L::kTileBytes + a * L::kAtomBytes, map,
-                        bar(L::kBarKVFull + slot), a * 64, si ? row0 : h_kv, si ? h_kv : row0, b,
-                        pol_kv);
+            tma_load_4d(sbase + L::kOffQ + t * L::kTileBytes + a * L::kAtomBytes, &p.tm_q,
+                        bar(L::kBarQFull + t), a * 64, si ? row0 : h, si ? h : row0, b, pol_q);
         }
-        ++kv_cnt;
+        ++q_cnt[t];
       }
+      if (!ok) break;
+      for (int j = 0; j < n_tiles && ok; ++j) {
+#pragma unroll
+        for (int kv = 0; kv < 2; ++kv) {
+          const uint32_t slot = kv_cnt % kStages;
+          const uint32_t ph = (kv_cnt / kStages) & 1u;
+          if (!sy.wait(bar(L::kBarKVEmpty + slot), ph ^ 1u, kSiteLoadKVEmpty)) { ok = false; break; }
+          if (leader) mbar_arrive_expect_tx(bar(L::kBarKVFull + slot), L::kTileBytes);
+          const CUtensorMap* map = kv ? &p.tm_v : &p.tm_k;
+          const bool si = (p.seq_inner_mask & (kv ? 4u : 2u)) != 0u;
+          const int row0 = j * 128;
+#pragma unroll
+          for (int a = 0; a < L::kAtoms; ++a) {
+            if (leader)
+              tma_load_4d(sbase + L::kOffKV + slot * L::kTileBytes + a * L::kAtomBytes, map,
+                          bar(L::kBarKVFull + slot), a * 64, si ? row0 : h_kv, si ? h_kv : row0, b,
+                          pol_kv);
+          }
+          ++kv_cnt;
+        }
+      }
+      if (!ok) break;
     }
-    if (!ok) break;
   }
   wq.finish();
   if (ok) return;
