@@ -31,7 +31,9 @@
 //
 // The MMA issue order  PV0(j-1), S0(j), PV1(j-1), S1(j)  lets warpgroup 0
 // run its softmax on S0(j) while the tensor core works on PV1(j-1) and S1(j),
-// and vice versa (ping-pong of the two Q tiles).
+// and vice versa (ping-pong of the two Q tiles).  The order runs on across
+// work items (except in the causal kernel at head_dim 128): the next item's
+// S0(0) goes between the current item's last PV0 and PV1.
 //
 // Numerics follow the reference (csrc/include/afa_softmax.cuh:12-127,
 // afa_forward_kernel.cuh:83-184): exp2 with log2(e) folded into the scale,
