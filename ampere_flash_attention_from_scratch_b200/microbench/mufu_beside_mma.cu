@@ -35,7 +35,14 @@ __device__ __forceinline__ float2 ffma2(float2 a, float2 b, float2 c) {
       : "l"(*reinterpret_cast<unsigned long long*>(&a)), "l"(*reinterpret_cast<unsigned long long*>(&b)),
         "l"(*reinterpret_cast<unsigned long long*>(&c))); return d; }
 
-// MIX: 0 ex2 x16 | 1 ex2 x16 + ffma2 x8 + cvt x8 | 2 ffma2 x16
+__device__ __forceinline__ float2 fadd2(float2 a, float2 b) {
+  float2 d; asm volatile("add.rn.f32x2 %0, %1, %2;" : "=l"(*reinterpret_cast<unsigned long long*>(&d))
+      : "l"(*reinterpret_cast<unsigned long long*>(&a)), "l"(*reinterpret_cast<unsigned long long*>(&b))); return d; }
+
+// MIX: 0 ex2 x16 | 1 ex2 x16 + ffma2 x8 + cvt x8 | 2 ffma2 x16 |
+//      3 the attention kernel's exponential loop over a 128-column row: per
+//        pair ffma2 (scale, subtract the max) -> 2 ex2 -> add.f32x2 (row sum)
+//        and cvt (pack P); 128 ex2 per iteration, reported per 16 ex2
 // KIND of the MMA stream: 0 SS N=128, D alternating between two accumulators
 // every 4 MMAs | 1 SS N=128, one accumulator | 2 TS N=128 (A from TMEM) |
 // 3 SS N=256 | 4 SS N=64
@@ -99,8 +106,25 @@ __global__ void __launch_bounds__(384, 1) bench(unsigned long long* cyc, unsigne
     }
     const float2 c2 = make_float2(0.999f, 1.0001f), d2 = make_float2(1e-7f, -1e-7f);
     uint32_t acc = 0;
+    float sc[128];
+    for (int i = 0; i < 128; ++i) sc[i] = -0.01f * i - threadIdx.x * 1e-4f;
     const unsigned long long t0 = clock64();
-    for (int it = 0; it < ITERS; ++it) {
+    if constexpr (MIX == 3) {
+      float2 a0 = make_float2(0.f, 0.f), a1 = a0;
+      const float2 nm = make_float2(-0.5f, -0.5f);
+      for (int it = 0; it < ITERS / 8; ++it) {
+#pragma unroll
+        for (int k = 0; k < 128; k += 2) {
+          const float2 x = ffma2(make_float2(sc[k], sc[k + 1]), c2, nm);
+          const float2 e = make_float2(ex2f(x.x), ex2f(x.y));
+          if ((k >> 1) & 1) a1 = fadd2(a1, e); else a0 = fadd2(a0, e);
+          acc ^= cvtbf(e.x, e.y);
+        }
+        sc[0] += a0.x * 1e-30f;  // a loop-carried use (the asm statements are volatile)
+      }
+      v[0] = a0.x + a0.y + a1.x + a1.y;
+    }
+    for (int it = 0; it < (MIX == 3 ? 0 : ITERS); ++it) {
 #pragma unroll
       for (int i = 0; i < 16; ++i) {
         if (MIX == 0 || MIX == 1) v[i] = ex2f(v[i]) - 1.0f;
@@ -172,5 +196,9 @@ int main() {
   run<2, true, 1>("ffma2 x16, MMAs queued", sms);
   run<2, false, 2>("ffma2 x16, tensor core idle", sms);
   run<2, true, 2>("ffma2 x16, MMAs queued", sms);
+  run<3, false, 1>("kernel exp loop, tensor core idle", sms);
+  run<3, true, 1>("kernel exp loop, MMAs queued", sms);
+  run<3, false, 2>("kernel exp loop, tensor core idle", sms);
+  run<3, true, 2>("kernel exp loop, MMAs queued", sms);
   return 0;
 }
