@@ -83,6 +83,10 @@ struct FwdParams {
   int n_kv;        // ceil(seq_len_kv / 128)
   int n_work;      // batch * n_heads * n_q_pairs
   int causal_off;  // seq_len_kv - seq_len: query row i sees keys j <= i + causal_off
+  // Division by n_q_pairs and by n_heads as a multiply and shift (see
+  // DivMagic): floor(x / d) = (x * mul) >> shift for 0 <= x < 2^31.
+  unsigned long long qp_mul, h_mul;
+  int qp_shift, h_shift;
   float* lse;      // optional [batch, n_heads, seq_len] fp32 log-sum-exp (natural log)
   int* sched;      // optional scheduler words [2] (causal kernel): 0 at rest; null = static schedule
   float scale_log2;  // scale * log2(e)
@@ -332,13 +336,33 @@ __device__ __forceinline__ float2 exp2_fma_pipe2(float2 x) {
 // the order, so the CTAs working at one time share the K/V of a few heads in
 // L2.  With a causal mask, q-pairs run from the last (longest) to the first,
 // so the round-robin assignment hands out long items first.
+// Division of a non-negative int below 2^31 by an invariant divisor d >= 1
+// (the round-up method of Granlund and Montgomery, "Division by invariant
+// integers using multiplication", 1994): with l = ceil(log2 d), p = 31 + l and
+// m = ceil(2^p / d) (at most 2^32), floor(x / d) = floor(x * m / 2^p) for every
+// 0 <= x < 2^31, since x * (m - 2^p / d) / 2^p < 2^31 / 2^p <= 1 / d.
+struct DivMagic {
+  unsigned long long mul;
+  int shift;
+  __host__ __device__ static DivMagic make(int d) {
+    int l = 0;
+    while ((1ll << l) < d) ++l;
+    const int sh = 31 + l;
+    return DivMagic{((1ull << sh) + static_cast<unsigned long long>(d) - 1ull) / static_cast<unsigned long long>(d), sh};
+  }
+};
+
+__device__ __forceinline__ int div_magic(int x, unsigned long long mul, int shift) {
+  return static_cast<int>((static_cast<unsigned long long>(static_cast<unsigned>(x)) * mul) >> shift);
+}
+
 template <bool kCausal>
 __device__ __forceinline__ void decode_work(const FwdParams& p, int w, int& qp, int& h, int& b) {
-  qp = w % p.n_q_pairs;
+  const int bh = div_magic(w, p.qp_mul, p.qp_shift);
+  qp = w - bh * p.n_q_pairs;
   if (kCausal) qp = p.n_q_pairs - 1 - qp;
-  const int bh = w / p.n_q_pairs;
-  h = bh % p.n_heads;
-  b = bh / p.n_heads;
+  b = div_magic(bh, p.h_mul, p.h_shift);
+  h = bh - b * p.n_heads;
 }
 
 // The work items a CTA processes, in order.  Static: blockIdx.x, then every
