@@ -643,7 +643,7 @@ __device__ __forceinline__ void role_mma(const FwdParams& p, uint32_t sbase, uin
   // its epilogue instead of after Q tile 1's last softmax and PV (the item
   // boundary of short sequences).  Its K_0 can load by then: of the ring only
   // the last V is still held.  Not in the causal kernel at head_dim 128,
-  // where it measured 0.2-0.5 % slower (+0.8-3.3 % at head_dim 64).
+  // where it measured 0.3-1.3 % slower (+0.8-3.3 % at head_dim 64).
 #ifndef AFA_EAGER_S0
 #define AFA_EAGER_S0 1
 #endif
@@ -660,8 +660,7 @@ __device__ __forceinline__ void role_mma(const FwdParams& p, uint32_t sbase, uin
     have_next = false;
     if (w < 0) break;  // done, or aborted
     // Q tile 0 visits n0 K/V tiles, Q tile 1 n1 >= n0 (equal without a causal
-    // mask; the work item is only decoded when they can differ, since this
-    // warp's integer divisions delay the item's first MMA).
+    // mask; the work item is only decoded when they can differ).
     int n0 = p.n_kv, n1 = p.n_kv;
     if (kCausal) {
       int qp, h, b;
